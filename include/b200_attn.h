@@ -1,0 +1,121 @@
+/*
+ * b200_attn.h — C ABI of the sm_100a fused attention forward.
+ *
+ * This is the drop-in boundary for the reference's attention operator.  Every
+ * entry point takes plain pointers, sizes and strides (no framework types) so a
+ * Python ctypes stub, a C++ host or any other FFI can bind it.
+ *
+ * Semantics follow the reference operator
+ *   triton_fused_attention(q, k, v, valid_token_mask, causal, scale, output_bshd)
+ *   (model/triton_fused_attention.py:1877-1891), whose value definition is
+ *   _reference_attention (model/triton_fused_attention.py:1256-1285):
+ *     scores = (q @ k^T) * scale
+ *     scores[i, j] = -inf  where causal and j > i            (triu(1) mask, :1273-1279)
+ *     scores[:, j] = -inf  where valid_token_mask[b, j] == 0  (key padding, :1280-1283)
+ *     out = softmax_fp32(scores).to(dtype) @ v               (:1284-1285)
+ *   A row whose keys are all masked yields NaN, as torch.softmax does.
+ *
+ * Tensors are [B, H, S, D] views whose last dimension is contiguous; the three
+ * outer strides are given in ELEMENTS and may describe transposed projection
+ * views ([B, S, H*D] seen as [B, H, S, D]) or a contiguous [B, S, H, D] output
+ * (the reference's output_bshd=True layout, :1950-1957).
+ */
+#ifndef B200_ATTN_H_
+#define B200_ATTN_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200_ATTN_API __attribute__((visibility("default")))
+#else
+#define B200_ATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_ATTN_ABI_VERSION 1
+
+/* Element types of q, k, v and the output. */
+enum {
+  B200_ATTN_DTYPE_BF16 = 0,
+  B200_ATTN_DTYPE_FP16 = 1
+};
+
+/* Return codes.  Entry points never abort the process. */
+enum {
+  B200_ATTN_OK = 0,
+  B200_ATTN_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, non-positive scale   */
+  B200_ATTN_ERR_UNSUPPORTED = 2,      /* dtype / head_dim outside the kernel envelope */
+  B200_ATTN_ERR_ALIGNMENT = 3,        /* base or stride not 16-byte aligned            */
+  B200_ATTN_ERR_DEVICE = 4,           /* no sm_100 device, or pointer not on a device  */
+  B200_ATTN_ERR_LAUNCH = 5,           /* CUDA launch / tensor-map encoding failed      */
+  B200_ATTN_ERR_TIMEOUT = 6           /* device reported a pipeline wait timeout      */
+};
+
+/* Bits the kernel ORs into *error_word (when error_word != NULL). */
+enum {
+  B200_ATTN_DEVERR_WAIT_TIMEOUT = 1
+};
+
+typedef struct b200_attn_fwd_params {
+  const void* q;           /* [B,H,S,D] */
+  const void* k;           /* [B,H,S,D] */
+  const void* v;           /* [B,H,S,D] */
+  void* o;                 /* [B,H,S,D] view of the output */
+  int64_t batch;
+  int64_t heads;
+  int64_t seq_len;
+  int64_t head_dim;
+  /* strides in elements: {batch, head, seq}; the D stride must be 1 */
+  int64_t q_stride[3];
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  /* optional bool [B,S] key-validity mask (1 = valid key), NULL = no mask */
+  const uint8_t* key_mask;
+  int64_t mask_stride[2];  /* {batch, seq} in bytes */
+  float scale;             /* softmax scale, > 0 (reference default D**-0.5) */
+  int32_t dtype;           /* B200_ATTN_DTYPE_* */
+  int32_t causal;          /* 1: key j visible to query i iff j <= i (top-left aligned) */
+  int32_t zero_masked_queries; /* 1: rows whose own mask bit is 0 are written as 0 */
+  int32_t* error_word;     /* optional device int; kernel ORs B200_ATTN_DEVERR_* */
+} b200_attn_fwd_params;
+
+/* ABI version (B200_ATTN_ABI_VERSION). */
+B200_ATTN_API int32_t b200_attn_abi_version(void);
+
+/* Host-only envelope query used by the planner: 1 when the kernel supports
+ * (dtype, head_dim) for the given causal/mask flags, else 0.  Makes no CUDA call.
+ * Replaces the support test of triton_fused_attention
+ * (model/triton_fused_attention.py:1906-1921) and the planner's envelope
+ * (model/attention_dispatch.py:399-459). */
+B200_ATTN_API int32_t b200_attn_query(int32_t dtype, int64_t head_dim, int32_t causal, int32_t has_mask);
+
+/* Host-only argument validation (shape, dtype, alignment, strides).  Returns a
+ * B200_ATTN_* code and makes no CUDA call.  Replaces _validate_inputs
+ * (model/triton_fused_attention.py:1217-1253) for the device path. */
+B200_ATTN_API int32_t b200_attn_check(const b200_attn_fwd_params* p);
+
+/* Launch the forward on `stream` (a cudaStream_t; NULL = legacy default stream).
+ * Asynchronous: no device synchronisation, no allocation.  Replaces the kernel
+ * launch of triton_fused_attention (model/triton_fused_attention.py:1968-2001). */
+B200_ATTN_API int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream);
+
+/* Static text for a return code. */
+B200_ATTN_API const char* b200_attn_error_string(int32_t code);
+
+/* Number of kernel launches b200_attn_fwd issues per call for these params
+ * (host-only; used by benchmarks to count launches). */
+B200_ATTN_API int32_t b200_attn_launches_per_call(const b200_attn_fwd_params* p);
+
+/* Text of the last host-side failure on the calling thread (CUDA error string,
+ * tensor-map encoding failure); empty when none. */
+B200_ATTN_API const char* b200_attn_last_error_detail(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_ATTN_H_ */

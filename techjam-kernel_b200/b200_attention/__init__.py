@@ -1,0 +1,8 @@
+"""B200 (sm_100a) fused attention forward behind the reference's attention API.
+
+- ``b200_fused_attention``: functional operator (reference: triton_fused_attention)
+- ``attention_dispatch``: planner (reference: model/attention_dispatch.py)
+- ``B200FusedSelfAttention``: module adapter (reference: TritonFusedSelfAttention)
+"""
+
+from .fused_attention import b200_fused_attention, read_device_errors  # noqa: F401

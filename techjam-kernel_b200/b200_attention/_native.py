@@ -1,0 +1,107 @@
+"""ctypes binding of the C ABI in ``include/b200_attn.h``.
+
+This module is torch-free: it loads ``libb200_attention.so`` and describes the
+parameter struct.  The library is loaded from this directory only; a missing or
+stale library is an error, never a reason to compute elsewhere.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libb200_attention.so"
+
+DTYPE_BF16 = 0
+DTYPE_FP16 = 1
+
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_UNSUPPORTED = 2
+ERR_ALIGNMENT = 3
+ERR_DEVICE = 4
+ERR_LAUNCH = 5
+ERR_TIMEOUT = 6
+
+DEVERR_WAIT_TIMEOUT = 1
+
+# Every symbol the header declares; the CPU test checks the library exports them.
+EXPORTED_SYMBOLS = (
+    "b200_attn_abi_version",
+    "b200_attn_query",
+    "b200_attn_check",
+    "b200_attn_fwd",
+    "b200_attn_error_string",
+    "b200_attn_launches_per_call",
+    "b200_attn_last_error_detail",
+)
+
+
+class FwdParams(ctypes.Structure):
+    """Mirror of ``b200_attn_fwd_params``."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("o", ctypes.c_void_p),
+        ("batch", ctypes.c_int64),
+        ("heads", ctypes.c_int64),
+        ("seq_len", ctypes.c_int64),
+        ("head_dim", ctypes.c_int64),
+        ("q_stride", ctypes.c_int64 * 3),
+        ("k_stride", ctypes.c_int64 * 3),
+        ("v_stride", ctypes.c_int64 * 3),
+        ("o_stride", ctypes.c_int64 * 3),
+        ("key_mask", ctypes.c_void_p),
+        ("mask_stride", ctypes.c_int64 * 2),
+        ("scale", ctypes.c_float),
+        ("dtype", ctypes.c_int32),
+        ("causal", ctypes.c_int32),
+        ("zero_masked_queries", ctypes.c_int32),
+        ("error_word", ctypes.c_void_p),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load_library() -> ctypes.CDLL:
+    """Load the native library (once).  Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH.name} is not built; run `python -m b200_attention.build` "
+                "or __graft_entry__.build()"
+            )
+        lib = ctypes.CDLL(str(LIB_PATH))
+        lib.b200_attn_abi_version.restype = ctypes.c_int32
+        lib.b200_attn_abi_version.argtypes = []
+        lib.b200_attn_query.restype = ctypes.c_int32
+        lib.b200_attn_query.argtypes = [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32]
+        lib.b200_attn_check.restype = ctypes.c_int32
+        lib.b200_attn_check.argtypes = [ctypes.POINTER(FwdParams)]
+        lib.b200_attn_fwd.restype = ctypes.c_int32
+        lib.b200_attn_fwd.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_void_p]
+        lib.b200_attn_error_string.restype = ctypes.c_char_p
+        lib.b200_attn_error_string.argtypes = [ctypes.c_int32]
+        lib.b200_attn_launches_per_call.restype = ctypes.c_int32
+        lib.b200_attn_launches_per_call.argtypes = [ctypes.POINTER(FwdParams)]
+        lib.b200_attn_last_error_detail.restype = ctypes.c_char_p
+        lib.b200_attn_last_error_detail.argtypes = []
+        _lib = lib
+        return lib
+
+
+def error_text(code: int) -> str:
+    lib = load_library()
+    text = lib.b200_attn_error_string(int(code)).decode()
+    detail = lib.b200_attn_last_error_detail().decode()
+    return f"{text} ({detail})" if detail and code in (ERR_DEVICE, ERR_LAUNCH) else text

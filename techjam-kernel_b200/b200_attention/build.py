@@ -1,0 +1,84 @@
+"""Build the sm_100a attention library in-tree with nvcc.
+
+The shared library is torch-free: it exports the C ABI declared in
+``include/b200_attn.h`` and links the CUDA runtime statically, so the same file
+serves the ctypes binding here and any other FFI host.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+from pathlib import Path
+
+PACKAGE_DIR = Path(__file__).resolve().parent
+PRODUCT_DIR = PACKAGE_DIR.parent
+REPO_ROOT = PRODUCT_DIR.parent
+CSRC = PRODUCT_DIR / "csrc"
+INCLUDE = REPO_ROOT / "include"
+LIB_NAME = "libb200_attention.so"
+LIB_PATH = PACKAGE_DIR / LIB_NAME
+
+SOURCES = ("attn_fwd_sm100.cu",)
+HEADERS = ("sm100_ptx.cuh",)
+
+NVCC_FLAGS = (
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3",
+    "-std=c++17",
+    "-lineinfo",
+    "-Xcompiler", "-fPIC",
+    "-Xcompiler", "-fvisibility=hidden",
+    "-shared",
+)
+
+
+def _nvcc() -> str:
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    candidate = Path(cuda_home) / "bin" / "nvcc"
+    if candidate.exists():
+        return str(candidate)
+    found = shutil.which("nvcc")
+    if not found:
+        raise RuntimeError("nvcc not found; set CUDA_HOME")
+    return found
+
+
+def _inputs() -> list[Path]:
+    files = [CSRC / s for s in SOURCES] + [CSRC / h for h in HEADERS]
+    files.append(INCLUDE / "b200_attn.h")
+    return files
+
+
+def is_stale() -> bool:
+    if not LIB_PATH.exists():
+        return True
+    built = LIB_PATH.stat().st_mtime
+    return any(f.stat().st_mtime > built for f in _inputs())
+
+
+def build_native(force: bool = False, verbose: bool = False) -> Path:
+    """Compile ``libb200_attention.so`` next to this file (skipped when fresh)."""
+    if not force and not is_stale():
+        return LIB_PATH
+    tmp = LIB_PATH.with_suffix(".so.tmp")
+    cmd = [_nvcc(), *NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}",
+           *[str(CSRC / s) for s in SOURCES], "-o", str(tmp)]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+        print(" ".join(cmd))
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"nvcc failed ({proc.returncode}):\n{proc.stderr[-8000:]}")
+    if verbose and proc.stderr:
+        print(proc.stderr)
+    os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+if __name__ == "__main__":
+    import sys
+
+    build_native(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    print(LIB_PATH)

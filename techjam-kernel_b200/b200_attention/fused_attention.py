@@ -1,0 +1,225 @@
+"""Functional attention operator over the sm_100a kernel.
+
+``b200_fused_attention`` keeps the signature, argument meaning and error
+behaviour of the reference operator ``triton_fused_attention``
+(model/triton_fused_attention.py:1877-1891): ``q, k, v`` are ``[B, H, S, D]``
+tensors with a contiguous last dimension (transposed projection views are
+consumed through their strides), ``valid_token_mask`` is an optional bool
+``[B, S]`` key mask, ``causal`` is top-left aligned, ``scale`` defaults to
+``D ** -0.5`` and must be positive, and ``output_bshd`` selects a contiguous
+``[B, S, H, D]`` output instead of ``[B, H, S, D]``.
+
+One deliberate difference: the reference silently falls back to dense PyTorch
+for inputs its kernels do not cover (:1906-1925).  This operator has no fallback
+of any kind; inputs outside the kernel envelope raise ``ValueError`` whatever
+``strict`` says.  Choosing an exact PyTorch path for such inputs is the
+planner's decision (``attention_dispatch``), made visibly, not the operator's.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from typing import Optional
+
+import torch
+
+from . import _native
+
+SUPPORTED_DTYPES = {torch.bfloat16: _native.DTYPE_BF16, torch.float16: _native.DTYPE_FP16}
+SUPPORTED_HEAD_DIMS = (64, 128)
+BLOCK_M = 128  # query rows per tile (two tiles per CTA)
+BLOCK_N = 128  # keys per K/V tile
+
+_error_words: dict[int, torch.Tensor] = {}
+_error_lock = threading.Lock()
+
+
+def _validate_inputs(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    valid_token_mask: Optional[torch.Tensor],
+) -> tuple[int, int, int, int]:
+    """Common tensor contract; same checks and exception types as the reference
+    (model/triton_fused_attention.py:1217-1253)."""
+    if q.ndim != 4:
+        raise ValueError(f"q must have shape [B, H, S, D], got {tuple(q.shape)}")
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(
+            "q, k, and v must have the same [B, H, S, D] shape; "
+            f"got q={tuple(q.shape)}, k={tuple(k.shape)}, v={tuple(v.shape)}"
+        )
+    if q.device != k.device or q.device != v.device:
+        raise ValueError("q, k, and v must be on the same device")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise TypeError("q, k, and v must have the same dtype")
+    if not q.dtype.is_floating_point:
+        raise TypeError(f"q/k/v must use a floating-point dtype, got {q.dtype}")
+    batch, heads, seq_len, head_dim = q.shape
+    if seq_len <= 0 or head_dim <= 0:
+        raise ValueError("sequence length and head dimension must be positive")
+    if valid_token_mask is not None:
+        if valid_token_mask.shape != (batch, seq_len):
+            raise ValueError(
+                "valid_token_mask must have shape "
+                f"{(batch, seq_len)}, got {tuple(valid_token_mask.shape)}"
+            )
+        if valid_token_mask.dtype != torch.bool:
+            raise TypeError("valid_token_mask must have dtype torch.bool")
+        if valid_token_mask.device != q.device:
+            raise ValueError("valid_token_mask and q must be on the same device")
+    return batch, heads, seq_len, head_dim
+
+
+def unsupported_reason(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Optional[str]:
+    """Why the sm_100a kernel cannot run these inputs, or None when it can."""
+    if q.device.type != "cuda":
+        return "inputs must be CUDA tensors"
+    if q.dtype not in SUPPORTED_DTYPES:
+        return f"dtype {q.dtype} is outside the kernel envelope (bfloat16, float16)"
+    if q.shape[-1] not in SUPPORTED_HEAD_DIMS:
+        return f"head_dim {q.shape[-1]} is outside the kernel envelope {SUPPORTED_HEAD_DIMS}"
+    if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
+        return "q/k/v must have a contiguous last dimension"
+    if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
+        return "the kernel is inference-only (autograd requested)"
+    major, _ = torch.cuda.get_device_capability(q.device)
+    if major != 10:
+        return f"the kernel is built for sm_100a; device capability is {major}.x"
+    return None
+
+
+def device_error_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 the kernel ORs error bits into (allocated once)."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    word = _error_words.get(index)
+    if word is None:
+        with _error_lock:
+            word = _error_words.get(index)
+            if word is None:
+                word = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+                _error_words[index] = word
+    return word
+
+
+def read_device_errors(device: torch.device, clear: bool = True) -> int:
+    """Synchronise and return the error bits the kernel reported on ``device``."""
+    word = device_error_word(device)
+    value = int(word.item())
+    if clear and value:
+        word.zero_()
+    return value
+
+
+def _strides(t: torch.Tensor) -> tuple[int, int, int]:
+    return (t.stride(0), t.stride(1), t.stride(2))
+
+
+def make_params(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    out_bhsd: torch.Tensor,
+    valid_token_mask: Optional[torch.Tensor],
+    causal: bool,
+    scale: float,
+    zero_masked_queries: bool,
+    error_word: Optional[torch.Tensor],
+) -> _native.FwdParams:
+    """Fill the C parameter struct from tensors (``out_bhsd`` is a [B,H,S,D] view)."""
+    batch, heads, seq_len, head_dim = q.shape
+    p = _native.FwdParams()
+    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), out_bhsd.data_ptr()
+    p.batch, p.heads, p.seq_len, p.head_dim = batch, heads, seq_len, head_dim
+    p.q_stride[:] = _strides(q)
+    p.k_stride[:] = _strides(k)
+    p.v_stride[:] = _strides(v)
+    p.o_stride[:] = _strides(out_bhsd)
+    if valid_token_mask is not None:
+        p.key_mask = valid_token_mask.data_ptr()
+        p.mask_stride[:] = (valid_token_mask.stride(0), valid_token_mask.stride(1))
+    p.scale = float(scale)
+    p.dtype = SUPPORTED_DTYPES[q.dtype]
+    p.causal = 1 if causal else 0
+    p.zero_masked_queries = 1 if zero_masked_queries else 0
+    p.error_word = error_word.data_ptr() if error_word is not None else None
+    return p
+
+
+def b200_fused_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    valid_token_mask: Optional[torch.Tensor] = None,
+    causal: bool = False,
+    scale: Optional[float] = None,
+    output_bshd: bool = False,
+    *,
+    strict: bool = False,
+    block_m: Optional[int] = None,
+    block_n: Optional[int] = None,
+    num_warps: Optional[int] = None,
+    num_stages: Optional[int] = None,
+    zero_masked_queries: bool = False,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Attention forward on the sm_100a kernel without materialising S x S.
+
+    Returns a new ``[B, H, S, D]`` tensor (or contiguous ``[B, S, H, D]`` with
+    ``output_bshd``).  ``zero_masked_queries`` additionally writes zeros for query
+    rows whose own mask bit is False (the value the reference's module produces
+    for them after its output projection, :2460-2461); it skips all work for
+    query blocks that lie entirely past the last valid key.  ``out`` may supply
+    the output tensor (same shape/dtype/device, contiguous last dim).
+
+    ``block_m``/``block_n`` are accepted for signature compatibility; the kernel
+    uses fixed 128 x 128 tiles and rejects other values.  ``num_warps`` and
+    ``num_stages`` are accepted and ignored (the kernel's warp roles and ring
+    depth are fixed per head dimension).  ``strict`` is accepted; unsupported
+    inputs always raise.
+    """
+    batch, heads, seq_len, head_dim = _validate_inputs(q, k, v, valid_token_mask)
+    if scale is None:
+        scale = head_dim**-0.5
+    if scale <= 0.0:
+        raise ValueError("scale must be positive")
+    if block_m not in (None, BLOCK_M) or block_n not in (None, BLOCK_N):
+        raise ValueError(f"the sm_100a kernel uses {BLOCK_M}x{BLOCK_N} tiles")
+    reason = unsupported_reason(q, k, v)
+    if reason is not None:
+        raise ValueError(f"unsupported sm_100a attention invocation: {reason}")
+    if zero_masked_queries and valid_token_mask is None:
+        raise ValueError("zero_masked_queries requires valid_token_mask")
+
+    if output_bshd:
+        shape = (batch, seq_len, heads, head_dim)
+        if out is None:
+            out = torch.empty(shape, device=q.device, dtype=q.dtype)
+        elif tuple(out.shape) != shape:
+            raise ValueError(f"out must have shape {shape}")
+        out_bhsd = out.transpose(1, 2)
+    else:
+        shape = (batch, heads, seq_len, head_dim)
+        if out is None:
+            out = torch.empty(shape, device=q.device, dtype=q.dtype)
+        elif tuple(out.shape) != shape:
+            raise ValueError(f"out must have shape {shape}")
+        out_bhsd = out
+    if out.dtype != q.dtype or out.device != q.device or out_bhsd.stride(-1) != 1:
+        raise ValueError("out must match q's dtype and device with a contiguous last dim")
+
+    lib = _native.load_library()
+    params = make_params(
+        q, k, v, out_bhsd, valid_token_mask, causal, scale, zero_masked_queries,
+        device_error_word(q.device),
+    )
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    rc = lib.b200_attn_fwd(ctypes.byref(params), ctypes.c_void_p(stream))
+    if rc == _native.ERR_INVALID_ARGUMENT or rc == _native.ERR_ALIGNMENT:
+        raise ValueError(f"b200_attn_fwd: {_native.error_text(rc)}")
+    if rc == _native.ERR_UNSUPPORTED:
+        raise ValueError(f"unsupported sm_100a attention invocation: {_native.error_text(rc)}")
+    if rc != _native.OK:
+        raise RuntimeError(f"b200_attn_fwd: {_native.error_text(rc)}")
+    return out
