@@ -1,0 +1,464 @@
+#!/usr/bin/env python3
+"""Benchmark of the sm_100a fused attention forward (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg2]
+    python bench.py --impl reference ...      # reference's CPU attention path
+
+A step is one attention forward over one batch of the workload (one kernel
+launch).  ``value`` is whole-job TFLOP/s with inputs resident in HBM; ``e2e``
+is the same metric through the public operator with pinned host buffers and
+the host<->device copies inside the timed region.  Multi-GPU runs use one
+process per GPU (torchrun); each rank owns an independent (batch x head)
+shard, there is no collective on the data path, and the time is the max over
+ranks.  Inputs rotate over several buffers whose total exceeds the 126 MB L2.
+
+FLOPs follow the algorithmic count 4*B*H*S^2*D (QK^T and PV), halved for
+causal; for the key-padded workload only valid (query, key) pairs count,
+4*H*D*sum(L_b^2), since padded query blocks are skipped.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT / "techjam-kernel_b200", ROOT):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "fused-attn fwd TFLOP/s & % bf16 tensor peak at 1/2/4/8 B200; vs CPU ms"
+UNIT = "TFLOP/s"
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# BASELINE configs (configs[1] is the default workload; "ns" is the north-star shape).
+WORKLOADS = {
+    "cfg1": dict(B=2, H=8, S=512, D=64, causal=True, masked=False, shard="batch"),
+    "cfg2": dict(B=8, H=16, S=2048, D=128, causal=True, masked=False, shard="batch"),
+    "cfg3": dict(B=16, H=32, S=4096, D=128, causal=False, masked=True, shard="batch"),
+    "cfg4": dict(B=1, H=32, S=32768, D=128, causal=True, masked=False, shard="heads"),
+    "ns": dict(B=8, H=16, S=8192, D=128, causal=True, masked=False, shard="batch"),
+}
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def valid_lengths(cfg: dict, seed: int) -> list[int] | None:
+    """Per-sequence valid lengths ~ U{S/4..S} from the seed (cfg3)."""
+    if not cfg["masked"]:
+        return None
+    import torch
+
+    gen = torch.Generator("cpu").manual_seed(seed + 7)
+    S = cfg["S"]
+    return torch.randint(S // 4, S + 1, (cfg["B"],), generator=gen).tolist()
+
+
+def flops_for(cfg: dict, batch: int, heads: int, lengths: list[int] | None) -> float:
+    S, D = cfg["S"], cfg["D"]
+    if lengths is not None:
+        return 4.0 * heads * D * float(sum(L * L for L in lengths))
+    f = 4.0 * batch * heads * S * S * D
+    return f / 2 if cfg["causal"] else f
+
+
+def shard_for(cfg: dict, world: int, rank: int) -> tuple[int, int, str]:
+    """(batch, heads) this rank processes and the scaling kind.
+
+    Weak scaling: every rank runs the full per-GPU workload (a data-parallel
+    job of N x B sequences).  Strong scaling (cfg4): the H heads are split in
+    contiguous ranges over the ranks (4 heads per GPU at N = 8)."""
+    if cfg["shard"] == "heads":
+        H = cfg["H"]
+        lo = (H * rank) // world
+        hi = (H * (rank + 1)) // world
+        return cfg["B"], hi - lo, "strong"
+    return cfg["B"], cfg["H"], "weak"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons via NVML while the timed region runs."""
+
+    REASONS = {
+        0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
+    }
+
+    def __init__(self, device_index: int, interval_s: float = 0.005):
+        self.interval = interval_s
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self.ok = False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self._nvml = None
+
+    def _run(self):
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(self.interval)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "source": "nvml" if self.ok else "unavailable"}
+        mhz = [s[0] for s in self.samples]
+        mask = 0
+        for _, r in self.samples:
+            mask |= r
+        reasons = sorted(name for bit, name in self.REASONS.items() if mask & bit)
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(mhz), "source": "nvml"}
+
+
+class CpuReference:
+    """The reference's CPU attention path timed on a bounded slice of the workload.
+
+    The timed call is the oracle's restatement of _reference_attention (torch CPU
+    ops in the reference's operation order, model/triton_fused_attention.py:1256-1285)
+    with all host threads.  The slice is one batch entry and enough heads for
+    ~0.1-0.5 s per call; for S > 8192 it is the last 512 query rows of one head
+    (the heaviest causal rows) through the bounded row form.
+    """
+
+    def __init__(self, cfg: dict, seed: int = 1234):
+        import torch
+
+        from oracle import reference_attention as ora
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.torch, self.ora = torch, ora
+        S, D, causal = cfg["S"], cfg["D"], cfg["causal"]
+        self.S, self.D, self.causal = S, D, causal
+        heads = max(1, min(cfg["H"], int(2 ** 31 // (S * S * 12))))
+        gen = torch.Generator("cpu").manual_seed(seed)
+        self.q, self.k, self.v = (torch.randn((1, heads, S, D), generator=gen).to(torch.bfloat16)
+                                  for _ in range(3))
+        lengths = valid_lengths(cfg, seed)
+        self.mask = None
+        self.rows = None
+        if S > 8192:
+            self.rows = (S - 512, S)
+            visible = sum((r + 1) if causal else S for r in range(*self.rows))
+            self.flop = 4.0 * heads * D * visible
+        elif lengths is not None:
+            L = lengths[0]
+            self.mask = torch.arange(S)[None, :] < L
+            self.flop = 4.0 * heads * D * L * L
+        else:
+            self.flop = flops_for(cfg, 1, heads, None)
+        self.desc = (f"oracle.reference_attention (torch CPU, bf16, reference op order) on "
+                     f"[1,{heads},{S},{D}] causal={causal}"
+                     + (f" rows {self.rows[0]}..{self.rows[1] - 1}" if self.rows else "")
+                     + (f" key-mask L={lengths[0]}" if self.mask is not None else "")
+                     + f"; {self.flop / 1e9:.2f} GFLOP per sample")
+        self.call()  # warm-up
+
+    def call(self) -> float:
+        t0 = time.perf_counter()
+        if self.rows is not None:
+            self.ora.reference_attention_rows(self.q, self.k, self.v, None, self.causal,
+                                              self.D ** -0.5, *self.rows)
+        else:
+            self.ora.reference_attention(self.q, self.k, self.v, self.mask, self.causal, self.D ** -0.5)
+        return time.perf_counter() - t0
+
+    def measure(self, budget_s: float, min_reps: int = 1) -> dict:
+        times = []
+        while sum(times) < budget_s or len(times) < min_reps:
+            times.append(self.call())
+        med = statistics.median(times)
+        return {"value": self.flop / med / 1e12, "unit": UNIT,
+                "cores": self.torch.get_num_threads(), "kind": "port",
+                "ms_per_sample": med * 1e3, "sample": f"{len(times)} reps of " + self.desc}
+
+
+def run_reference_arm(args, cfg: dict, rank: int, world: int) -> int:
+    """Reference arm: the reference's CPU attention on host cores, rank 0 only."""
+    if rank != 0:
+        return 0
+    ref = CpuReference(cfg, args.seed)
+    for _ in range(args.warmup):
+        ref.call()
+    times = [ref.call() for _ in range(args.steps)]
+    ms = statistics.median(times) * 1e3
+    value = ref.flop / (ms * 1e-3) / 1e12
+    line = {
+        "impl": "reference",
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak" if cfg["shard"] != "heads" else "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded torch.randn N(0,1))",
+        "config": {"workload": args.workload, **{k: cfg[k] for k in ("B", "H", "S", "D", "causal")},
+                   "impl_path": "oracle.reference_attention on host CPU cores"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": ref.torch.get_num_threads(),
+                         "kind": "port", "sample": f"{args.steps} timed reps of " + ref.desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seed", type=int, default=1234)
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    cfg = WORKLOADS[args.workload]
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return run_reference_arm(args, cfg, rank, world)
+
+    import torch
+    import torch.distributed as dist
+
+    from b200_attention import _native
+    from b200_attention.fused_attention import (b200_fused_attention, device_error_word,
+                                                read_device_errors)
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    B, H, scaling = shard_for(cfg, world, rank)
+    S, D, causal = cfg["S"], cfg["D"], cfg["causal"]
+    lengths = valid_lengths(cfg, args.seed)
+    flop_rank = flops_for(cfg, B, H, lengths)
+    tot = torch.tensor([flop_rank], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tot)
+    flop_job = float(tot.item())
+
+    # ---- inputs: rotate over enough buffers that their total exceeds L2
+    bytes_per_set = 4 * B * H * S * D * 2
+    n_sets = max(2, math.ceil(2 * L2_BYTES / bytes_per_set))
+    gen = torch.Generator(device=dev).manual_seed(args.seed + 1000 * rank)
+    sets = []
+    for _ in range(n_sets):
+        q, k, v = (torch.randn((B, H, S, D), generator=gen, device=dev, dtype=torch.float32)
+                   .to(torch.bfloat16) for _ in range(3))
+        sets.append((q, k, v))
+    mask = None
+    if lengths is not None:
+        mask = (torch.arange(S, device=dev)[None, :] <
+                torch.tensor(lengths, device=dev)[:, None])
+    outs = [torch.empty((B, S, H, D), device=dev, dtype=torch.bfloat16) for _ in range(n_sets)]
+    zero_q = mask is not None
+
+    def step(i):
+        q, k, v = sets[i % n_sets]
+        return b200_fused_attention(q, k, v, mask, causal, output_bshd=True,
+                                    zero_masked_queries=zero_q, out=outs[i % n_sets])
+
+    stream = torch.cuda.current_stream(dev)
+    # W warm-up steps, continued until ~0.5 s of work so clocks leave idle
+    t_w = time.perf_counter()
+    i = 0
+    while i < args.warmup or time.perf_counter() - t_w < 0.5:
+        step(i)
+        i += 1
+        if i % 8 == 0:
+            torch.cuda.synchronize(dev)
+    torch.cuda.synchronize(dev)
+    if read_device_errors(dev):
+        raise RuntimeError("kernel reported a device error during warm-up")
+
+    # ---- device-resident timed region
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    sampler = ClockSampler(local_rank)
+    barrier()
+    torch.cuda.synchronize(dev)
+    with sampler:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            step(i)
+            ev[i][1].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    elapsed_ms = max_over_ranks(t_start.elapsed_time(t_end))
+    launch_ms = [a.elapsed_time(b) for a, b in ev]
+    avg_launch_ms = statistics.mean(launch_ms)
+    errors = read_device_errors(dev)
+    ms_per_step = elapsed_ms / args.steps
+    value = flop_job / (ms_per_step * 1e-3) / 1e12
+    achieved = flop_rank / (avg_launch_ms * 1e-3) / 1e12  # this rank's kernel, per launch
+
+    # ---- validation gather (outside the timed region): finiteness and a checksum per rank
+    o = outs[(args.steps - 1) % n_sets].float()
+    finite = torch.isfinite(o).all()
+    check = torch.stack([o.abs().sum(dtype=torch.float64), finite.double(),
+                         torch.tensor(float(errors), device=dev, dtype=torch.float64)])
+    gathered = [torch.zeros_like(check) for _ in range(world)]
+    if world > 1:
+        dist.all_gather(gathered, check)
+    else:
+        gathered = [check]
+    validation = {"finite_all_ranks": all(bool(g[1].item()) for g in gathered),
+                  "device_errors": int(sum(g[2].item() for g in gathered)),
+                  "checksums": [round(float(g[0].item()), 3) for g in gathered]}
+
+    # ---- end to end through the public operator with pinned host buffers
+    e2e_steps = args.e2e_steps or max(3, min(args.steps, 20))
+    hq, hk, hv = (t.cpu().pin_memory() for t in sets[0])
+    hmask = mask.cpu().pin_memory() if mask is not None else None
+    hout = torch.empty((B, S, H, D), dtype=torch.bfloat16).pin_memory()
+    h2d = 3 * hq.numel() * hq.element_size() + (hmask.numel() if hmask is not None else 0)
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step():
+        q = hq.to(dev, non_blocking=True)
+        k = hk.to(dev, non_blocking=True)
+        v = hv.to(dev, non_blocking=True)
+        m = hmask.to(dev, non_blocking=True) if hmask is not None else None
+        o = b200_fused_attention(q, k, v, m, causal, output_bshd=True, zero_masked_queries=zero_q)
+        hout.copy_(o, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
+    e2e_value = flop_job / (e2e_ms * 1e-3) / 1e12
+
+    # ---- CPU baseline (rank 0, N = 1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = CpuReference(cfg, args.seed).measure(args.cpu_budget, min_reps=3)
+
+    peaks, peak_src = load_peaks()
+    peak = peaks["bf16_tflops"]
+    traffic = None
+    prof = ROOT / "profiles" / f"attn_fwd_sm100_{args.workload}_traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
+    lib = _native.load_library()
+    launches = args.steps  # one kernel launch per step (b200_attn_launches_per_call == 1)
+
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": scaling,
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded torch.randn N(0,1), no dataset)",
+        "config": {
+            "workload": args.workload, "B": cfg["B"], "H": cfg["H"], "S": S, "D": D,
+            "causal": causal, "key_padding": lengths is not None,
+            "per_rank_batch_heads": [B, H],
+            "parallelism": f"{'bxh' if scaling == 'weak' else 'heads'}-shard x{world}, no data-path collective",
+            "l2": f"inputs rotated over {n_sets} buffer sets of {bytes_per_set / 2**20:.0f} MiB (> L2)",
+            "flop_per_step_job": flop_job,
+            "valid_lengths": lengths,
+        },
+        "pct_of_bf16_peak": 100.0 * value / (peak * world),
+        "roofline": {
+            "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak, "traffic": traffic,
+            "peak_source": f"{peak_src} bf16_tflops (burst, kernel timed alone)",
+            "avg_launch_ms": avg_launch_ms,
+        },
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": launches,
+        "clocks": sampler.summary(),
+        "validation": validation,
+    }
+    if cpu:
+        line["speedup_vs_cpu_e2e"] = e2e_value / cpu["value"]
+    print(json.dumps(line), flush=True)
+    _ = lib, device_error_word
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

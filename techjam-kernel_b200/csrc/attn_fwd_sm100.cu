@@ -54,12 +54,18 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O when the max grows by > 2^8
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;
 constexpr float kLog2e = 1.4426950408889634f;
+#ifndef B200_ATTN_POLY_PER8
+#define B200_ATTN_POLY_PER8 0
+#endif
+// Of every 8 probabilities, this many are computed with the FMA-pipe exp2.
+constexpr int kPolyPer8 = B200_ATTN_POLY_PER8;
 
 struct KernelArgs {
   int32_t seq_len;
   int32_t heads;
   int32_t batch;
   int32_t num_q_blocks;  // ceil(S / 256)
+  float scale;           // softmax scale
   float scale_log2;      // scale * log2(e)
   int32_t zero_masked_queries;
   const uint8_t* mask;   // [B,S] bool or null
@@ -104,6 +110,37 @@ __device__ __forceinline__ int warp_max_i(int v) {
 #pragma unroll
   for (int off = 16; off; off >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, off));
   return v;
+}
+
+// x rounded to the input dtype and widened back to fp32.
+template <bool BF16>
+__device__ __forceinline__ float round_to_input(float x) {
+  if constexpr (BF16) {
+    return __bfloat162float(__float2bfloat16_rn(x));
+  } else {
+    return __half2float(__float2half_rn(x));
+  }
+}
+
+// Three-input maximum (sm_100 max.f32 with three sources).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x on the FMA pipe, for -126 <= x <= 64.  x = n + f with n = rint(x)
+// obtained by adding 1.5*2^23 (the sum's low mantissa bits hold n, f in
+// [-0.5, 0.5]); 2^f from a degree-3 polynomial fitted here by a Remez
+// iteration for minimax relative error on [-0.5, 0.5] (max 7.5e-5, below the
+// 2^-9 rounding of the 16-bit probabilities); 2^n is added to the exponent
+// field as (bits(x + 1.5*2^23) << 23), whose high bits shift out.
+__device__ __forceinline__ float ex2_poly(float x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  const float t = x + kRound;
+  const float f = x - (t - kRound);
+  const float p = fmaf(fmaf(fmaf(0.05517167f, f, 0.24261113f), f, 0.69326097f), f, 0.99992806f);
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
 }
 
 // Bounded wait on an mbarrier phase.  Returns false when the CTA was aborted
@@ -409,11 +446,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tmem_wait_ld();
 
       const bool edge = (key0 + kBlockN > S);
-      if (kMask || edge || (kCausal && j == diag)) {
-        if constexpr (kMask) {
+      bool partial = edge || (kCausal && j == diag);
+      if constexpr (kMask) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) mw[q] = __ballot_sync(0xffffffffu, mb[q] != 0);
-        }
+        for (int q = 0; q < 4; ++q) mw[q] = __ballot_sync(0xffffffffu, mb[q] != 0);
+        partial = partial || ((mw[0] & mw[1] & mw[2] & mw[3]) != ~0u);
+      }
+      if (partial) {
         int lim = S - 1 - key0;  // last in-range key of this tile
         if (kCausal && j == diag) lim = min(lim, rl);
 #pragma unroll
@@ -426,11 +465,72 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
       }
 
-      float mx = -INFINITY;
+      if (n == 1) {
+        // Every visible key of this query tile lies in this one key tile, so
+        // the row sum is complete here: reproduce the reference's rounding
+        // points exactly (model/triton_fused_attention.py:1272-1284): scores
+        // rounded to the input dtype, the scale multiply rounded again, fp32
+        // softmax normalised before P is rounded.  Rows with few keys (early
+        // causal rows, short or heavily padded sequences) have large outputs,
+        // where a different rounding order would show as whole output ulps.
+        const float scale = args.scale;
+        float cmx[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 4; ++c) {
+          float m4 = -INFINITY;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[c][e]));
+          for (int e = 0; e < 32; ++e) {
+            const float v = round_to_input<kBF16>(round_to_input<kBF16>(__uint_as_float(sr[c][e])) * scale);
+            sr[c][e] = __float_as_uint(v);
+            m4 = fmaxf(m4, v);
+          }
+          cmx[c] = m4;
+        }
+        const float mx2 = fmaxf(fmaxf(cmx[0], cmx[1]), fmaxf(cmx[2], cmx[3]));
+        const float sub = (mx2 == -INFINITY) ? 0.f : mx2;
+        float tot = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float pe = expf(__uint_as_float(sr[c][e]) - sub);
+            sr[c][e] = __float_as_uint(pe);
+            tot += pe;
+          }
+        const float inv = 1.f / tot;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            pk[e] = pack2<kBF16>(__uint_as_float(sr[c][2 * e]) * inv,
+                                 __uint_as_float(sr[c][2 * e + 1]) * inv);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) sr[c >> 1][16 * (c & 1) + e] = pk[e];
+          if (c & 1) ptx::tmem_st_32x32b_x32(tP + 32 * (c >> 1), sr[c >> 1]);
+        }
+        m_run = mx2;  // -inf only when the row has no visible key (NaN output)
+        l_run = 1.f;  // P is already normalised
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(p_full(i));
+        continue;
+      }
+
+      // Row max: a 3-input max tree (depth 5) instead of a 128-long chain.
+      float cm[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[11];
+#pragma unroll
+        for (int t = 0; t < 10; ++t)
+          v[t] = fmax3(__uint_as_float(sr[c][3 * t]), __uint_as_float(sr[c][3 * t + 1]),
+                       __uint_as_float(sr[c][3 * t + 2]));
+        v[10] = fmaxf(__uint_as_float(sr[c][30]), __uint_as_float(sr[c][31]));
+        cm[c] = fmax3(fmax3(v[0], v[1], v[2]), fmax3(v[3], v[4], v[5]),
+                      fmax3(v[6], v[7], fmax3(v[8], v[9], v[10])));
+      }
+      const float mx = fmaxf(fmaxf(cm[0], cm[1]), fmaxf(cm[2], cm[3]));
       const float m_cand = mx * scale_log2;
       const bool resc = m_cand > m_run + kRescaleLog2;
       const float m_new = resc ? m_cand : m_run;
@@ -439,25 +539,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       m_run = m_new;
       const float neg_m = (m_run == -INFINITY) ? 0.f : -m_run;
 
-      float sum0 = 0.f, sum1 = 0.f;
+      // p = 2^(s*scale*log2e - m): most elements on the MUFU (ex2.approx),
+      // kPolyPer8 of every 8 on the FMA pipe (ex2_poly), which balances the
+      // two pipes; four independent partial sums.
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = ptx::ex2_approx(fmaf(__uint_as_float(sr[c][2 * e]), scale_log2, neg_m));
-          const float p1 =
-              ptx::ex2_approx(fmaf(__uint_as_float(sr[c][2 * e + 1]), scale_log2, neg_m));
-          sum0 += p0;
-          sum1 += p1;
-          pk[e] = pack2<kBF16>(p0, p1);
+          float p2[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int k = 2 * e + h;
+            const float x = fmaf(__uint_as_float(sr[c][k]), scale_log2, neg_m);
+            p2[h] = ((k & 7) < kPolyPer8) ? ex2_poly(fmaxf(x, -126.f)) : ptx::ex2_approx(x);
+          }
+          sum[e & 3] += p2[0] + p2[1];
+          pk[e] = pack2<kBF16>(p2[0], p2[1]);
         }
         // pack two 16-column groups into one 32-column store
 #pragma unroll
         for (int e = 0; e < 16; ++e) sr[c >> 1][16 * (c & 1) + e] = pk[e];
         if (c & 1) ptx::tmem_st_32x32b_x32(tP + 32 * (c >> 1), sr[c >> 1]);
       }
-      l_run += sum0 + sum1;
+      l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
 
       if (j > 0 && __any_sync(0xffffffffu, resc)) {
         // O_i holds sum over tiles < j (its last MMA completed before S_i(j)).
@@ -494,7 +600,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (args.zero_masked_queries && row < S)
           zero_row = mrow[static_cast<int64_t>(row) * args.mask_ss] == 0;
       }
-      const float inv_l = zero_row ? 0.f : 1.f / l_run;
+      // a row that saw no visible key is NaN, as torch.softmax of all -inf
+      const float inv_l = zero_row ? 0.f : (m_run == -INFINITY ? __int_as_float(0x7fc00000) : 1.f / l_run);
       const uint32_t stage = sbase + C::kOffQ + i * C::kTileBytes;  // Q_i is no longer read
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -751,6 +858,7 @@ extern "C" int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream) {
   a.heads = static_cast<int32_t>(p->heads);
   a.batch = static_cast<int32_t>(p->batch);
   a.num_q_blocks = static_cast<int32_t>((p->seq_len + kRowsPerCta - 1) / kRowsPerCta);
+  a.scale = p->scale;
   a.scale_log2 = p->scale * kLog2e;
   a.zero_masked_queries = p->zero_masked_queries;
   a.mask = p->key_mask;

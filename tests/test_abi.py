@@ -1,0 +1,134 @@
+"""C ABI checks that need no GPU: exports, struct layout, host-side validation.
+
+The library must export every function ``include/b200_attn.h`` declares; the
+ctypes mirror of ``b200_attn_fwd_params`` must match the C layout (compiled
+here with gcc); ``b200_attn_check`` / ``b200_attn_query`` answer without any
+CUDA call.
+"""
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from b200_attention import _native
+from b200_attention.attention_dispatch import SM100_HEAD_DIMS
+from b200_attention.build import LIB_PATH, build_native
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "b200_attn.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build_native()  # no-op when the in-tree library is fresh
+    return _native.load_library()
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return re.findall(r"B200_ATTN_API\s+[\w\s\*]+?\b(b200_attn_\w+)\s*\(", text)
+
+
+def test_header_declarations_are_mirrored():
+    names = declared_functions()
+    assert names, "no declarations parsed"
+    assert set(names) == set(_native.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", str(LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT\s+(b200_attn_\w+)", out))
+    for name in declared_functions():
+        assert name in exported, name
+        assert hasattr(lib, name)
+
+
+def test_params_struct_layout_matches_c(tmp_path):
+    fields = [f for f, _ in _native.FwdParams._fields_]
+    src = tmp_path / "layout.c"
+    body = "\n".join(f'  printf("{f} %zu\\n", offsetof(b200_attn_fwd_params, {f}));' for f in fields)
+    src.write_text(f'#include <stdio.h>\n#include <stddef.h>\n#include "b200_attn.h"\n'
+                   f'int main(void) {{\n  printf("size %zu\\n", sizeof(b200_attn_fwd_params));\n{body}\n  return 0;\n}}\n')
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", f"-I{ROOT / 'include'}", str(src), "-o", str(exe)], check=True)
+    lines = dict(l.split() for l in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                   check=True).stdout.splitlines())
+    assert int(lines["size"]) == ctypes.sizeof(_native.FwdParams)
+    for f in fields:
+        assert int(lines[f]) == getattr(_native.FwdParams, f).offset, f
+
+
+def test_abi_version(lib):
+    assert lib.b200_attn_abi_version() == 1
+
+
+def test_query_agrees_with_planner_envelope(lib):
+    for dtype in (_native.DTYPE_BF16, _native.DTYPE_FP16, 7):
+        for d in (16, 32, 64, 96, 128, 256):
+            want = 1 if dtype in (0, 1) and d in SM100_HEAD_DIMS else 0
+            assert lib.b200_attn_query(dtype, d, 1, 0) == want
+
+
+def _params(**kw):
+    p = _native.FwdParams()
+    base = 0x10000
+    p.q, p.k, p.v, p.o = base, base + 0x100000, base + 0x200000, base + 0x300000
+    p.batch, p.heads, p.seq_len, p.head_dim = 2, 4, 256, 128
+    st = (4 * 256 * 128, 256 * 128, 128)
+    for name in ("q_stride", "k_stride", "v_stride", "o_stride"):
+        getattr(p, name)[:] = st
+    p.scale = 128 ** -0.5
+    p.dtype = _native.DTYPE_BF16
+    for k, v in kw.items():
+        setattr(p, k, v)
+    return p
+
+
+def _check(lib, p):
+    return lib.b200_attn_check(ctypes.byref(p))
+
+
+def test_check_accepts_valid_params(lib):
+    assert _check(lib, _params()) == _native.OK
+    assert lib.b200_attn_launches_per_call(ctypes.byref(_params())) == 1
+    # transposed projection view: [B,S,H,D] storage seen as [B,H,S,D]
+    p = _params()
+    for name in ("q_stride", "k_stride", "v_stride"):
+        getattr(p, name)[:] = (256 * 4 * 128, 128, 4 * 128)
+    assert _check(lib, p) == _native.OK
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(q=None), _native.ERR_INVALID_ARGUMENT),
+    (dict(batch=0), _native.ERR_INVALID_ARGUMENT),
+    (dict(seq_len=0), _native.ERR_INVALID_ARGUMENT),
+    (dict(scale=0.0), _native.ERR_INVALID_ARGUMENT),
+    (dict(scale=-1.0), _native.ERR_INVALID_ARGUMENT),
+    (dict(scale=float("inf")), _native.ERR_INVALID_ARGUMENT),
+    (dict(dtype=5), _native.ERR_UNSUPPORTED),
+    (dict(head_dim=96), _native.ERR_UNSUPPORTED),
+    (dict(head_dim=32), _native.ERR_UNSUPPORTED),
+    (dict(q=0x10008), _native.ERR_ALIGNMENT),
+    (dict(zero_masked_queries=1), _native.ERR_INVALID_ARGUMENT),
+])
+def test_check_rejects(lib, kw, code):
+    assert _check(lib, _params(**kw)) == code
+
+
+def test_check_rejects_unaligned_stride(lib):
+    p = _params()
+    p.k_stride[:] = (4 * 256 * 128, 256 * 128, 132)  # 264-byte rows: not a 16-byte multiple
+    assert _check(lib, p) == _native.ERR_ALIGNMENT
+    p = _params(seq_len=1)
+    p.k_stride[:] = (4 * 1 * 128, 128, 3)  # seq stride irrelevant when S == 1
+    assert _check(lib, p) == _native.OK
+
+
+def test_error_strings(lib):
+    for code in range(7):
+        assert lib.b200_attn_error_string(code)
+    assert b"unknown" in lib.b200_attn_error_string(99)
