@@ -6,18 +6,22 @@
 // the input dtype, times v.  Fully masked rows give NaN like torch.softmax.
 //
 // Work decomposition.  One CTA owns 256 query rows of one (batch, head) as two
-// 128-row tiles Q0, Q1 and streams 128-key K/V tiles through a shared-memory
-// ring.  Ten warps, each with one job:
+// 128-row tiles Q0, Q1 and streams BN-key K/V tiles (BN = 64 for D = 128,
+// 128 for D = 64) through a shared-memory ring.  Ten warps, one job each:
 //   warps 0-3  softmax for Q0 (one thread per query row = one TMEM lane)
 //   warps 4-7  softmax for Q1
 //   warp  8    TMA producer (Q once, then K_j, V_j into the ring)
 //   warp  9    tcgen05 issuer (one elected thread) and TMEM owner
-// Tensor memory (512 columns x 128 lanes, fp32 cells):
-//   [0,128)   S0 = Q0 K_j^T      (P0 as packed 16-bit pairs in [64,128))
-//   [128,256) S1 = Q1 K_j^T      (P1 in [192,256))
-//   [256,256+D) O0, [256+D,256+2D) O1  (fp32 accumulators)
-// MMA issue order per key tile j: PV0(j-1), QK0(j), PV1(j-1), QK1(j), so the
-// tensor core works on one query tile while the other tile's softmax runs.
+// Tensor memory (512 columns x 128 lanes of 32 bit) holds the scores
+// S = Q_i K_j^T (BN fp32 columns), one buffer of P_i per query tile (BN/2
+// columns of packed 16-bit pairs) and the fp32 accumulators O_i (D columns):
+//   D = 128: S (128, shared by Q0 and Q1) | P0 P1 (2x64) | O0 O1 (2x128) = 512
+//   D =  64: S0 S1 (2x128)                | P0 P1 (2x64) | O0 O1 (2x64)  = 512
+// P never aliases S, so a QK product only waits until the previous scores in
+// its S buffer were copied to registers by their softmax warpgroup, never for
+// a PV product; PV_i(j) is issued once P_i(j) is written.  Both softmax
+// warpgroups then run their tiles back to back while the tensor core computes
+// the next scores and the previous PV products.
 // The running max is updated lazily: O and the row sum are rescaled only when
 // the max grows by more than 2^8, which keeps the unnormalised P in range and
 // makes rescaling rare; the final O / l is exact either way.
@@ -43,13 +47,13 @@
 
 namespace b200attn {
 
-constexpr int kBlockM = 128;         // query rows per tile = TMEM lanes
-constexpr int kBlockN = 128;         // keys per K/V tile
+constexpr int kBlockM = 128;  // query rows per tile = TMEM lanes
 constexpr int kRowsPerCta = 2 * kBlockM;
 constexpr int kSoftmaxWarps = 8;
 constexpr int kLoadWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kQkWarp = 9;   // issues QK products, owns TMEM
+constexpr int kPvWarp = 10;  // issues PV products
+constexpr int kThreads = 352;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O when the max grows by > 2^8
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;
@@ -76,22 +80,52 @@ struct KernelArgs {
   int32_t* err;
 };
 
-template <int D, int NSLOT>
+// Compile-time shape of one kernel instance.
+template <int D_, int BN_, int PB_, int NSLOT_, bool SHARED_S_>
 struct Cfg {
+  static constexpr int D = D_;          // head dim
+  static constexpr int BN = BN_;        // keys per K/V tile
+  static constexpr int PB = PB_;        // P buffers per query tile
+  static constexpr int NSLOT = NSLOT_;  // K/V ring slots (one K or V tile each)
+  static constexpr bool kSharedS = SHARED_S_;  // one S buffer for both query tiles
+  static constexpr int kSBufs = kSharedS ? 1 : 2;
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
-  static constexpr int kChunks = D / 64;               // 128-byte swizzle chunks per row
-  static constexpr int kChunkBytes = kBlockM * 128;    // one chunk of a 128-row tile
-  static constexpr int kTileBytes = kBlockM * D * 2;   // Q, K or V tile
+  static_assert(BN == 64 || BN == 128, "BN 64 or 128");
+  static constexpr int kChunks = D / 64;              // 128-byte swizzle chunks per row
+  static constexpr int kQChunkBytes = kBlockM * 128;  // one chunk of a 128-row tile
+  static constexpr int kKVChunkBytes = BN * 128;      // one chunk of a BN-row tile
+  static constexpr int kQTileBytes = kBlockM * D * 2;
+  static constexpr int kKVTileBytes = BN * D * 2;
   static constexpr int kOffQ = 0;
-  static constexpr int kOffRing = 2 * kTileBytes;
-  static constexpr int kOffBar = kOffRing + NSLOT * kTileBytes;
-  // q_full, slot_full[NSLOT], slot_empty[NSLOT], s_full[2], p_full[2], o_full[2], drain
-  static constexpr int kNumBars = 1 + 2 * NSLOT + 7;
+  static constexpr int kOffRing = 2 * kQTileBytes;
+  static constexpr int kOffBar = kOffRing + NSLOT * kKVTileBytes;
+  // barrier indices
+  static constexpr int kBarQ = 0;
+  static constexpr int kBarSlotFull = 1;
+  static constexpr int kBarSlotEmpty = kBarSlotFull + NSLOT;
+  static constexpr int kBarSFull = kBarSlotEmpty + NSLOT;  // [2]
+  static constexpr int kBarSFree = kBarSFull + 2;          // [2]
+  static constexpr int kBarPFull = kBarSFree + 2;          // [2][PB]
+  static constexpr int kBarPVDone = kBarPFull + 2 * PB;    // [2][PB]
+  static constexpr int kBarOFull = kBarPVDone + 2 * PB;    // [2]
+  static constexpr int kBarDrain = kBarOFull + 2;
+  static constexpr int kNumBars = kBarDrain + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 16 + 1024;  // + alignment slack
-  // TMEM column of S_i (P_i lives in its upper 64 columns) and of O_i
-  __host__ __device__ static constexpr uint32_t col_s(int i) { return 128u * i; }
-  __host__ __device__ static constexpr uint32_t col_o(int i) { return 256u + D * i; }
+  static_assert(kSmemBytes <= 232448, "exceeds the 227 KB per-block shared memory limit");
+  // TMEM columns
+  __host__ __device__ static constexpr uint32_t col_s(int i) { return kSharedS ? 0u : BN * i; }
+  __host__ __device__ static constexpr uint32_t col_p(int i, int b) {
+    return kSBufs * BN + (i * PB + b) * (BN / 2);
+  }
+  __host__ __device__ static constexpr uint32_t col_o(int i) {
+    return kSBufs * BN + PB * BN + D * i;
+  }
+  static_assert(kSBufs * BN + PB * BN + 2 * D <= 512, "TMEM budget");
+  // Query tiles whose visible keys all lie in the first kExactKeys keys take
+  // the exact-rounding path (keys held in registers across <= 2 tiles).
+  static constexpr int kExactKeys = 128;
+  static constexpr int kExactTiles = kExactKeys / BN;
 };
 
 // ---------------------------------------------------------------- helpers
@@ -104,12 +138,6 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
   }
-}
-
-__device__ __forceinline__ int warp_max_i(int v) {
-#pragma unroll
-  for (int off = 16; off; off >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, off));
-  return v;
 }
 
 // x rounded to the input dtype and widened back to fp32.
@@ -143,10 +171,38 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
 }
 
+// Max of N consecutive values (N a multiple of 32) as a 3-input tree.
+template <int N>
+__device__ __forceinline__ float row_max(const uint32_t (&s)[N]) {
+  static_assert(N % 32 == 0, "chunks of 32");
+  float cm[N / 32];
+#pragma unroll
+  for (int c = 0; c < N / 32; ++c) {
+    float v[11];
+#pragma unroll
+    for (int t = 0; t < 10; ++t)
+      v[t] = fmax3(__uint_as_float(s[32 * c + 3 * t]), __uint_as_float(s[32 * c + 3 * t + 1]),
+                   __uint_as_float(s[32 * c + 3 * t + 2]));
+    v[10] = fmaxf(__uint_as_float(s[32 * c + 30]), __uint_as_float(s[32 * c + 31]));
+    cm[c] = fmax3(fmax3(v[0], v[1], v[2]), fmax3(v[3], v[4], v[5]),
+                  fmax3(v[6], v[7], fmax3(v[8], v[9], v[10])));
+  }
+  float m = cm[0];
+#pragma unroll
+  for (int c = 1; c < N / 32; ++c) m = fmaxf(m, cm[c]);
+  return m;
+}
+
+__device__ __forceinline__ int warp_max_i(int v) {
+#pragma unroll
+  for (int off = 16; off; off >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+
 // Bounded wait on an mbarrier phase.  Returns false when the CTA was aborted
 // (by this thread's timeout or another's).
-__device__ __noinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
-                                      int32_t* err) {
+__device__ __noinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity,
+                                           volatile uint32_t* abort_flag, int32_t* err) {
   const uint64_t t0 = ptx::globaltimer_ns();
   while (true) {
 #pragma unroll 1
@@ -175,6 +231,13 @@ __device__ __forceinline__ bool warp_wait_bar(uint32_t bar, uint32_t parity,
   const bool all = __all_sync(0xffffffffu, ok);
   if (!all) *abort_flag = 1u;
   return all;
+}
+
+// One arrival per warp after all lanes finished their tcgen05 accesses.
+__device__ __forceinline__ void warp_arrive(uint32_t bar, int lane) {
+  ptx::tc_fence_before();
+  __syncwarp();
+  if (lane == 0) ptx::mbar_arrive(bar);
 }
 
 // Last valid key + 1 of one mask row (0 when none).  One warp, scanning
@@ -207,14 +270,35 @@ __device__ int mask_extent(const uint8_t* mrow, int64_t ss, int S, int lane) {
   return last + 1;
 }
 
+// Load N fp32 score columns of this thread's row from TMEM.
+template <int N>
+__device__ __forceinline__ void load_row(uint32_t taddr, uint32_t (&s)[N]) {
+#pragma unroll
+  for (int c = 0; c < N / 32; ++c)
+    ptx::tmem_ld_32x32b_x32(taddr + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * c]));
+  ptx::tmem_wait_ld();
+}
+
+// Set scores of invisible keys to -inf: key k of the tile is visible iff
+// k <= lim and its mask bit is set.
+template <int N>
+__device__ __forceinline__ void mask_row(uint32_t (&s)[N], int lim, const uint32_t* mw) {
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    const bool vis = (k <= lim) && (((mw[k >> 5] >> (k & 31)) & 1u) != 0u);
+    if (!vis) s[k] = __float_as_uint(-INFINITY);
+  }
+}
+
 // ----------------------------------------------------------------- kernel
-template <int D, int NSLOT, bool kCausal, bool kMask, bool kBF16>
+template <class C, bool kCausal, bool kMask, bool kBF16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v,
                           const __grid_constant__ CUtensorMap tm_o, const KernelArgs args) {
-  using C = Cfg<D, NSLOT>;
+  constexpr int D = C::D, BN = C::BN, PB = C::PB, NSLOT = C::NSLOT;
+  constexpr int kMaskWords = BN / 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -234,14 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + C::kOffMisc);
   // misc[0] TMEM base, misc[1] abort flag, misc[2] key extent
   volatile uint32_t* abort_flag = misc + 1;
-  const uint32_t bar_base = sbase + C::kOffBar;
-  const uint32_t bar_q = bar_base;
-  auto slot_full = [&](uint32_t s) { return bar_base + 8u * (1u + s); };
-  auto slot_empty = [&](uint32_t s) { return bar_base + 8u * (1u + NSLOT + s); };
-  auto s_full = [&](int i) { return bar_base + 8u * (1u + 2u * NSLOT + i); };
-  auto p_full = [&](int i) { return bar_base + 8u * (3u + 2u * NSLOT + i); };
-  auto o_full = [&](int i) { return bar_base + 8u * (5u + 2u * NSLOT + i); };
-  const uint32_t bar_drain = bar_base + 8u * (7u + 2u * NSLOT);
+  const uint32_t bar0 = sbase + C::kOffBar;
+  auto bar = [&](int idx) { return bar0 + 8u * static_cast<uint32_t>(idx); };
 
   const uint8_t* mrow = nullptr;
   if constexpr (kMask) mrow = args.mask + static_cast<int64_t>(b) * args.mask_sb;
@@ -253,17 +331,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       misc[1] = 0u;
       misc[2] = static_cast<uint32_t>(extent);
-      ptx::mbar_init(bar_q, 1);
+      ptx::mbar_init(bar(C::kBarQ), 1);
       for (int s = 0; s < NSLOT; ++s) {
-        ptx::mbar_init(slot_full(s), 1);
-        ptx::mbar_init(slot_empty(s), 1);
+        ptx::mbar_init(bar(C::kBarSlotFull + s), 1);
+        ptx::mbar_init(bar(C::kBarSlotEmpty + s), 1);
       }
       for (int i = 0; i < 2; ++i) {
-        ptx::mbar_init(s_full(i), 1);
-        ptx::mbar_init(p_full(i), kBlockM);
-        ptx::mbar_init(o_full(i), 1);
+        ptx::mbar_init(bar(C::kBarSFull + i), 1);
+        ptx::mbar_init(bar(C::kBarSFree + i), 4);  // one arrival per softmax warp
+        for (int pb = 0; pb < PB; ++pb) {
+          // per P buffer, so neither barrier can complete twice unobserved:
+          // buffer b is rewritten only after PV on b completed
+          ptx::mbar_init(bar(C::kBarPFull + i * PB + pb), 4);
+          ptx::mbar_init(bar(C::kBarPVDone + i * PB + pb), 1);
+        }
+        ptx::mbar_init(bar(C::kBarOFull + i), 1);
       }
-      ptx::mbar_init(bar_drain, 1);
+      ptx::mbar_init(bar(C::kBarDrain), 2);  // one commit per issuing thread
       ptx::fence_mbar_init();
       ptx::fence_proxy_async_smem();
       ptx::tma_prefetch_desc(&tm_q);
@@ -291,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
 
-  if (warp == kMmaWarp) {
+  if (warp == kQkWarp) {
     ptx::tmem_alloc(sbase + C::kOffMisc, kTmemCols);
     ptx::tmem_relinquish();
   }
@@ -301,38 +385,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = misc[0];
 
   // Key tiles each query tile visits.
-  const int n_kv = kMask ? max(1, (extent + kBlockN - 1) / kBlockN) : (S + kBlockN - 1) / kBlockN;
+  const int kv_keys = kMask ? max(1, extent) : S;
+  const int n_kv = (kv_keys + BN - 1) / BN;
   int n_tiles[2];
 #pragma unroll
-  for (int i = 0; i < 2; ++i)
-    n_tiles[i] = kCausal ? min(2 * qb + i + 1, n_kv) : n_kv;
+  for (int i = 0; i < 2; ++i) {
+    const int q_end = q0 + kBlockM * (i + 1);  // one past the tile's last row
+    n_tiles[i] = kCausal ? min((q_end + BN - 1) / BN, n_kv) : n_kv;
+  }
   const int n_max = n_tiles[1];  // Q1 never needs fewer tiles than Q0
 
   if (warp == kLoadWarp) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
-      ptx::mbar_arrive_expect_tx(bar_q, 2u * C::kTileBytes);
+      ptx::mbar_arrive_expect_tx(bar(C::kBarQ), 2u * C::kQTileBytes);
 #pragma unroll
       for (int i = 0; i < 2; ++i)
 #pragma unroll
         for (int c = 0; c < C::kChunks; ++c)
-          ptx::tma_load_4d(sbase + C::kOffQ + i * C::kTileBytes + c * C::kChunkBytes, &tm_q, bar_q,
-                           64 * c, q0 + kBlockM * i, h, b);
+          ptx::tma_load_4d(sbase + C::kOffQ + i * C::kQTileBytes + c * C::kQChunkBytes, &tm_q,
+                           bar(C::kBarQ), 64 * c, q0 + kBlockM * i, h, b);
       uint32_t L = 0;
       bool ok = true;
       for (int j = 0; ok && j < n_max; ++j) {
         for (int kv = 0; kv < 2; ++kv) {
           const uint32_t s = L % NSLOT, r = L / NSLOT;
-          if (!wait_bar(slot_empty(s), (r & 1u) ^ 1u, abort_flag, args.err)) {
+          if (!wait_bar(bar(C::kBarSlotEmpty + s), (r & 1u) ^ 1u, abort_flag, args.err)) {
             ok = false;
             break;
           }
-          ptx::mbar_arrive_expect_tx(slot_full(s), C::kTileBytes);
+          ptx::mbar_arrive_expect_tx(bar(C::kBarSlotFull + s), C::kKVTileBytes);
           const CUtensorMap* tm = kv ? &tm_v : &tm_k;
 #pragma unroll
           for (int c = 0; c < C::kChunks; ++c)
-            ptx::tma_load_4d(sbase + C::kOffRing + s * C::kTileBytes + c * C::kChunkBytes, tm,
-                             slot_full(s), 64 * c, kBlockN * j, h, b);
+            ptx::tma_load_4d(sbase + C::kOffRing + s * C::kKVTileBytes + c * C::kKVChunkBytes, tm,
+                             bar(C::kBarSlotFull + s), 64 * c, BN * j, h, b);
           ++L;
         }
       }
@@ -341,249 +428,301 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t first = L > NSLOT ? L - NSLOT : 0u;
         for (uint32_t x = first; x < L; ++x) {
           const uint64_t t0 = ptx::globaltimer_ns();
-          while (!ptx::mbar_try_wait(slot_full(x % NSLOT), (x / NSLOT) & 1u) &&
+          while (!ptx::mbar_try_wait(bar(C::kBarSlotFull + x % NSLOT), (x / NSLOT) & 1u) &&
                  ptx::globaltimer_ns() - t0 < kWaitTimeoutNs) {
           }
         }
       }
     }
     __syncwarp();
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------ tcgen05 issuer
+  } else if (warp == kQkWarp) {
+    // -------------------------------------------- tcgen05 issuer: scores
+    // S_i(j) = Q_i K(j)^T: A = Q (K-major), B = K (K-major, BN rows).  A QK
+    // product may overwrite its S buffer once the previous scores in that
+    // buffer were copied to registers by their softmax warpgroup.  With one
+    // shared S buffer the occupancy order is S0(0), S1(0), S0(1), S1(1), ...
     if (lane == 0) {
-      constexpr uint32_t id_qk = ptx::idesc_f16(kBF16, kBlockM, kBlockN, false);
-      constexpr uint32_t id_pv = ptx::idesc_f16(kBF16, kBlockM, D, true);
-      bool ok = wait_bar(bar_q, 0, abort_flag, args.err);
-      for (int j = 0; ok && j <= n_max; ++j) {
-        const uint32_t kL = 2u * j, vL = 2u * j - 1u;  // K(j), V(j-1) load indices
-        const uint32_t ks = kL % NSLOT, vs = vL % NSLOT;
-        if (j < n_max && !wait_bar(slot_full(ks), (kL / NSLOT) & 1u, abort_flag, args.err)) {
-          ok = false;
-          break;
-        }
-        if (j >= 1 && !wait_bar(slot_full(vs), (vL / NSLOT) & 1u, abort_flag, args.err)) {
-          ok = false;
-          break;
-        }
-        ptx::tc_fence_after();
+      constexpr uint32_t id_qk = ptx::idesc_f16(kBF16, kBlockM, BN, false);
+      bool ok = wait_bar(bar(C::kBarQ), 0, abort_flag, args.err);
+      int prev_i[2] = {-1, -1}, prev_j[2] = {-1, -1};  // last occupant per S buffer
+      for (int j = 0; ok && j < n_max; ++j) {
+        const uint32_t kL = 2u * j, ks = kL % NSLOT;
+        ok = wait_bar(bar(C::kBarSlotFull + ks), (kL / NSLOT) & 1u, abort_flag, args.err);
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
-          if (j >= 1 && j - 1 < n_tiles[i]) {
-            // O_i += P_i(j-1) V(j-1): A = P from TMEM, B = V (MN-major, D contiguous)
-            if (!wait_bar(p_full(i), (j - 1) & 1, abort_flag, args.err)) {
-              ok = false;
-              break;
-            }
-            ptx::tc_fence_after();
-            const uint32_t vaddr = sbase + C::kOffRing + vs * C::kTileBytes;
-#pragma unroll
-            for (int kk = 0; kk < kBlockN / 16; ++kk) {
-              const uint64_t bdesc = ptx::smem_desc_sw128(vaddr + kk * 2048, C::kChunkBytes, 1024);
-              ptx::tc_mma_ts(tmem + C::col_o(i), tmem + C::col_s(i) + 64 + kk * 8, bdesc, id_pv,
-                             (j > 1 || kk > 0) ? 1u : 0u);
-            }
-            if (j - 1 == n_tiles[i] - 1) ptx::tc_commit(o_full(i));
-            if (i == 1) ptx::tc_commit(slot_empty(vs));
+          if (!ok || j >= n_tiles[i]) continue;
+          const int sb = C::kSharedS ? 0 : i;
+          if (prev_i[sb] >= 0 &&
+              !wait_bar(bar(C::kBarSFree + prev_i[sb]), prev_j[sb] & 1, abort_flag, args.err)) {
+            ok = false;
+            break;
           }
-          if (j < n_tiles[i]) {
-            // S_i = Q_i K(j)^T: A = Q (K-major), B = K (K-major)
-            const uint32_t qaddr = sbase + C::kOffQ + i * C::kTileBytes;
-            const uint32_t kaddr = sbase + C::kOffRing + ks * C::kTileBytes;
+          prev_i[sb] = i;
+          prev_j[sb] = j;
+          ptx::tc_fence_after();
+          const uint32_t qaddr = sbase + C::kOffQ + i * C::kQTileBytes;
+          const uint32_t kaddr = sbase + C::kOffRing + ks * C::kKVTileBytes;
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t off = (kk >> 2) * C::kChunkBytes + (kk & 3) * 32;
-              ptx::tc_mma_ss(tmem + C::col_s(i), ptx::smem_desc_sw128(qaddr + off, 16, 1024),
-                             ptx::smem_desc_sw128(kaddr + off, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
-            }
-            ptx::tc_commit(s_full(i));
-            if (i == 1) ptx::tc_commit(slot_empty(ks));
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t qo = (kk >> 2) * C::kQChunkBytes + (kk & 3) * 32;
+            const uint32_t ko = (kk >> 2) * C::kKVChunkBytes + (kk & 3) * 32;
+            ptx::tc_mma_ss(tmem + C::col_s(i), ptx::smem_desc_sw128(qaddr + qo, 16, 1024),
+                           ptx::smem_desc_sw128(kaddr + ko, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
           }
+          ptx::tc_commit(bar(C::kBarSFull + i));
         }
+        // Q1 is K(j)'s last reader (Q0 never needs more key tiles than Q1)
+        if (ok) ptx::tc_commit(bar(C::kBarSlotEmpty + ks));
       }
       // Drain: every MMA this thread issued completes before TMEM is freed.
-      ptx::tc_commit(bar_drain);
+      ptx::tc_commit(bar(C::kBarDrain));
       const uint64_t t0 = ptx::globaltimer_ns();
-      while (!ptx::mbar_try_wait(bar_drain, 0) && ptx::globaltimer_ns() - t0 < kWaitTimeoutNs) {
+      while (!ptx::mbar_try_wait(bar(C::kBarDrain), 0) &&
+             ptx::globaltimer_ns() - t0 < kWaitTimeoutNs) {
+      }
+    }
+    __syncwarp();
+  } else if (warp == kPvWarp) {
+    // --------------------------------------- tcgen05 issuer: PV products
+    // O_i += P_i(j) V(j): A = P from TMEM, B = V (MN-major, D contiguous),
+    // issued as soon as the softmax warpgroup has written P_i(j).
+    if (lane == 0) {
+      constexpr uint32_t id_pv = ptx::idesc_f16(kBF16, kBlockM, D, true);
+      bool ok = true;
+      for (int j = 0; ok && j < n_max; ++j) {
+        const uint32_t vL = 2u * j + 1u, vs = vL % NSLOT;
+        ok = wait_bar(bar(C::kBarSlotFull + vs), (vL / NSLOT) & 1u, abort_flag, args.err);
+        const uint32_t vaddr = sbase + C::kOffRing + vs * C::kKVTileBytes;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          if (!ok || j >= n_tiles[i]) continue;
+          if (!wait_bar(bar(C::kBarPFull + i * PB + (j % PB)), (j / PB) & 1, abort_flag,
+                        args.err)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t pcol = tmem + C::col_p(i, j % PB);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t bdesc =
+                ptx::smem_desc_sw128(vaddr + kk * 2048, C::kKVChunkBytes, 1024);
+            ptx::tc_mma_ts(tmem + C::col_o(i), pcol + kk * 8, bdesc, id_pv,
+                           (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          ptx::tc_commit(bar(C::kBarPVDone + i * PB + (j % PB)));
+          if (j == n_tiles[i] - 1) ptx::tc_commit(bar(C::kBarOFull + i));
+        }
+        if (ok) ptx::tc_commit(bar(C::kBarSlotEmpty + vs));  // Q1 is V(j)'s last reader
+      }
+      ptx::tc_commit(bar(C::kBarDrain));
+      const uint64_t t0 = ptx::globaltimer_ns();
+      while (!ptx::mbar_try_wait(bar(C::kBarDrain), 0) &&
+             ptx::globaltimer_ns() - t0 < kWaitTimeoutNs) {
       }
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
-    const int i = warp >> 2;                 // query tile
-    const int quad = warp & 3;               // TMEM lane quadrant of this warp
-    const int rl = quad * 32 + lane;         // row within the tile = TMEM lane
-    const int row = q0 + kBlockM * i + rl;   // global query row
+    const int i = warp >> 2;              // query tile
+    const int quad = warp & 3;            // TMEM lane quadrant of this warp
+    const int rl = quad * 32 + lane;      // row within the tile = TMEM lane
+    const int qstart = q0 + kBlockM * i;  // first row of the tile
+    const int row = qstart + rl;          // global query row
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t tS = tmem + lane_off + C::col_s(i);
-    const uint32_t tP = tS + 64;
     const uint32_t tO = tmem + lane_off + C::col_o(i);
     const float scale_log2 = args.scale_log2;
     const int n = n_tiles[i];
-    const int diag = kCausal ? 2 * qb + i : -1;
+    const uint32_t bar_s_full = bar(C::kBarSFull + i), bar_s_free = bar(C::kBarSFree + i);
+    auto bar_p_full = [&](int j) { return bar(C::kBarPFull + i * PB + (j % PB)); };
+
+    // mask bits of key tile j for the warp (all ones without a mask)
+    auto mask_words = [&](int j, uint32_t (&mw)[kMaskWords]) {
+#pragma unroll
+      for (int q = 0; q < kMaskWords; ++q) {
+        if constexpr (kMask) {
+          const int key = j * BN + 32 * q + lane;
+          const bool v = key < S && mrow[static_cast<int64_t>(key) * args.mask_ss] != 0;
+          mw[q] = __ballot_sync(0xffffffffu, v);
+        } else {
+          mw[q] = ~0u;
+        }
+      }
+    };
+    // largest visible in-tile key index given bounds and causality
+    auto visible_limit = [&](int j) {
+      const int key0 = j * BN;
+      int lim = S - 1 - key0;
+      if (kCausal) lim = min(lim, row - key0);
+      return lim;
+    };
+    auto partial_tile = [&](int j, const uint32_t (&mw)[kMaskWords]) {
+      const int key0 = j * BN;
+      bool p = key0 + BN > S || (kCausal && key0 + BN - 1 > qstart);
+      if constexpr (kMask) {
+        uint32_t all = ~0u;
+#pragma unroll
+        for (int q = 0; q < kMaskWords; ++q) all &= mw[q];
+        p = p || all != ~0u;
+      }
+      return p;
+    };
 
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      const int key0 = j * kBlockN;
-      uint32_t mw[4] = {~0u, ~0u, ~0u, ~0u};
-      uint8_t mb[4] = {1, 1, 1, 1};
-      if constexpr (kMask) {
+
+    if (n <= C::kExactTiles) {
+      // Every visible key of this query tile lies in the first 128 keys, so
+      // the whole row fits in registers: reproduce the reference's rounding
+      // points exactly (model/triton_fused_attention.py:1272-1284): scores
+      // rounded to the input dtype, the scale multiply rounded again, fp32
+      // softmax normalised before P is rounded.  These rows have few keys and
+      // large outputs, where a different rounding order would show as whole
+      // output ulps.
+      constexpr int NE = C::kExactKeys;
+      uint32_t sr[NE];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int key = key0 + 32 * q + lane;
-          mb[q] = key < S ? mrow[static_cast<int64_t>(key) * args.mask_ss] : uint8_t(0);
+      for (int k = 0; k < NE; ++k) sr[k] = __float_as_uint(-INFINITY);
+#pragma unroll
+      for (int j = 0; j < C::kExactTiles; ++j) {
+        if (j < n && ok) {
+          uint32_t mw[kMaskWords];
+          mask_words(j, mw);
+          if (!warp_wait_bar(bar_s_full, j & 1, abort_flag, args.err)) {
+            ok = false;
+          } else {
+            ptx::tc_fence_after();
+            uint32_t part[BN];
+            load_row<BN>(tS, part);
+            warp_arrive(bar_s_free, lane);
+            mask_row<BN>(part, visible_limit(j), mw);
+#pragma unroll
+            for (int k = 0; k < BN; ++k) sr[j * BN + k] = part[k];
+          }
         }
       }
-      if (!warp_wait_bar(s_full(i), j & 1, abort_flag, args.err)) {
-        ok = false;
-        break;
-      }
-      ptx::tc_fence_after();
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) ptx::tmem_ld_32x32b_x32(tS + 32 * c, sr[c]);
-      ptx::tmem_wait_ld();
-
-      const bool edge = (key0 + kBlockN > S);
-      bool partial = edge || (kCausal && j == diag);
-      if constexpr (kMask) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) mw[q] = __ballot_sync(0xffffffffu, mb[q] != 0);
-        partial = partial || ((mw[0] & mw[1] & mw[2] & mw[3]) != ~0u);
-      }
-      if (partial) {
-        int lim = S - 1 - key0;  // last in-range key of this tile
-        if (kCausal && j == diag) lim = min(lim, rl);
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int k = 32 * c + e;
-            const bool vis = (k <= lim) && (((mw[c] >> e) & 1u) != 0u);
-            if (!vis) sr[c][e] = __float_as_uint(-INFINITY);
-          }
-      }
-
-      if (n == 1) {
-        // Every visible key of this query tile lies in this one key tile, so
-        // the row sum is complete here: reproduce the reference's rounding
-        // points exactly (model/triton_fused_attention.py:1272-1284): scores
-        // rounded to the input dtype, the scale multiply rounded again, fp32
-        // softmax normalised before P is rounded.  Rows with few keys (early
-        // causal rows, short or heavily padded sequences) have large outputs,
-        // where a different rounding order would show as whole output ulps.
+      if (ok) {
         const float scale = args.scale;
-        float cmx[4];
+        float mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float m4 = -INFINITY;
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float v = round_to_input<kBF16>(round_to_input<kBF16>(__uint_as_float(sr[c][e])) * scale);
-            sr[c][e] = __float_as_uint(v);
-            m4 = fmaxf(m4, v);
-          }
-          cmx[c] = m4;
+        for (int k = 0; k < NE; ++k) {
+          const float v =
+              round_to_input<kBF16>(round_to_input<kBF16>(__uint_as_float(sr[k])) * scale);
+          sr[k] = __float_as_uint(v);
+          mx = fmaxf(mx, v);
         }
-        const float mx2 = fmaxf(fmaxf(cmx[0], cmx[1]), fmaxf(cmx[2], cmx[3]));
-        const float sub = (mx2 == -INFINITY) ? 0.f : mx2;
+        const float sub = (mx == -INFINITY) ? 0.f : mx;
         float tot = 0.f;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float pe = expf(__uint_as_float(sr[c][e]) - sub);
-            sr[c][e] = __float_as_uint(pe);
-            tot += pe;
-          }
+        for (int k = 0; k < NE; ++k) {
+          const float pe = expf(__uint_as_float(sr[k]) - sub);
+          sr[k] = __float_as_uint(pe);
+          tot += pe;
+        }
         const float inv = 1.f / tot;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
+        for (int j = 0; j < C::kExactTiles; ++j) {
+          if (j < n) {
+            uint32_t pk[BN / 2];
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            pk[e] = pack2<kBF16>(__uint_as_float(sr[c][2 * e]) * inv,
-                                 __uint_as_float(sr[c][2 * e + 1]) * inv);
+            for (int e = 0; e < BN / 2; ++e)
+              pk[e] = pack2<kBF16>(__uint_as_float(sr[j * BN + 2 * e]) * inv,
+                                   __uint_as_float(sr[j * BN + 2 * e + 1]) * inv);
+            const uint32_t tP = tmem + lane_off + C::col_p(i, j % PB);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) sr[c >> 1][16 * (c & 1) + e] = pk[e];
-          if (c & 1) ptx::tmem_st_32x32b_x32(tP + 32 * (c >> 1), sr[c >> 1]);
+            for (int c = 0; c < BN / 64; ++c)
+              ptx::tmem_st_32x32b_x32(tP + 32 * c,
+                                      *reinterpret_cast<uint32_t(*)[32]>(&pk[32 * c]));
+            ptx::tmem_wait_st();
+            warp_arrive(bar_p_full(j), lane);
+          }
         }
-        m_run = mx2;  // -inf only when the row has no visible key (NaN output)
+        m_run = mx;   // -inf only when the row has no visible key (NaN output)
         l_run = 1.f;  // P is already normalised
-        ptx::tmem_wait_st();
-        ptx::tc_fence_before();
-        ptx::mbar_arrive(p_full(i));
-        continue;
       }
+    } else {
+      for (int j = 0; j < n; ++j) {
+        uint32_t mw[kMaskWords];
+        mask_words(j, mw);
+        if (!warp_wait_bar(bar_s_full, j & 1, abort_flag, args.err)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        uint32_t sr[BN];
+        load_row<BN>(tS, sr);
+        warp_arrive(bar_s_free, lane);  // the MMA warp may now overwrite S_i
 
-      // Row max: a 3-input max tree (depth 5) instead of a 128-long chain.
-      float cm[4];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[11];
-#pragma unroll
-        for (int t = 0; t < 10; ++t)
-          v[t] = fmax3(__uint_as_float(sr[c][3 * t]), __uint_as_float(sr[c][3 * t + 1]),
-                       __uint_as_float(sr[c][3 * t + 2]));
-        v[10] = fmaxf(__uint_as_float(sr[c][30]), __uint_as_float(sr[c][31]));
-        cm[c] = fmax3(fmax3(v[0], v[1], v[2]), fmax3(v[3], v[4], v[5]),
-                      fmax3(v[6], v[7], fmax3(v[8], v[9], v[10])));
-      }
-      const float mx = fmaxf(fmaxf(cm[0], cm[1]), fmaxf(cm[2], cm[3]));
-      const float m_cand = mx * scale_log2;
-      const bool resc = m_cand > m_run + kRescaleLog2;
-      const float m_new = resc ? m_cand : m_run;
-      const float alpha = resc ? ptx::ex2_approx(m_run - m_new) : 1.f;
-      l_run *= alpha;
-      m_run = m_new;
-      const float neg_m = (m_run == -INFINITY) ? 0.f : -m_run;
+        if (partial_tile(j, mw)) mask_row<BN>(sr, visible_limit(j), mw);
 
-      // p = 2^(s*scale*log2e - m): most elements on the MUFU (ex2.approx),
-      // kPolyPer8 of every 8 on the FMA pipe (ex2_poly), which balances the
-      // two pipes; four independent partial sums.
-      float sum[4] = {0.f, 0.f, 0.f, 0.f};
+        const float m_cand = row_max<BN>(sr) * scale_log2;
+        const bool resc = m_cand > m_run + kRescaleLog2;
+        const float m_new = resc ? m_cand : m_run;
+        const float alpha = resc ? ptx::ex2_approx(m_run - m_new) : 1.f;
+        l_run *= alpha;
+        m_run = m_new;
+        const float neg_m = (m_run == -INFINITY) ? 0.f : -m_run;
+
+        // p = 2^(s*scale*log2e - m); kPolyPer8 of every 8 on the FMA pipe
+        // (ex2_poly), the rest on the MUFU; four independent partial sums.
+        float sum[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[BN / 2];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
+        for (int e = 0; e < BN / 2; ++e) {
           float p2[2];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int k = 2 * e + h;
-            const float x = fmaf(__uint_as_float(sr[c][k]), scale_log2, neg_m);
-            p2[h] = ((k & 7) < kPolyPer8) ? ex2_poly(fmaxf(x, -126.f)) : ptx::ex2_approx(x);
+          for (int hh = 0; hh < 2; ++hh) {
+            const int k = 2 * e + hh;
+            const float x = fmaf(__uint_as_float(sr[k]), scale_log2, neg_m);
+            p2[hh] = ((k & 7) < kPolyPer8) ? ex2_poly(fmaxf(x, -126.f)) : ptx::ex2_approx(x);
           }
           sum[e & 3] += p2[0] + p2[1];
           pk[e] = pack2<kBF16>(p2[0], p2[1]);
         }
-        // pack two 16-column groups into one 32-column store
-#pragma unroll
-        for (int e = 0; e < 16; ++e) sr[c >> 1][16 * (c & 1) + e] = pk[e];
-        if (c & 1) ptx::tmem_st_32x32b_x32(tP + 32 * (c >> 1), sr[c >> 1]);
-      }
-      l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
+        l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
 
-      if (j > 0 && __any_sync(0xffffffffu, resc)) {
-        // O_i holds sum over tiles < j (its last MMA completed before S_i(j)).
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          ptx::tmem_ld_32x32b_x32(tO + 32 * c, o);
-          ptx::tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          ptx::tmem_st_32x32b_x32(tO + 32 * c, o);
+        // P buffer j % PB was last read by PV_i(j - PB).
+        if (j >= PB) {
+          const int pb = j % PB;
+          if (!warp_wait_bar(bar(C::kBarPVDone + i * PB + pb), ((j / PB) + 1) & 1, abort_flag,
+                             args.err)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
         }
+        if (j > 0 && __any_sync(0xffffffffu, resc)) {
+          // O_i must hold the sum over tiles < j: wait for PV_i(j-1).
+          const int pb = (j - 1) % PB;
+          if (!warp_wait_bar(bar(C::kBarPVDone + i * PB + pb), ((j - 1) / PB) & 1, abort_flag,
+                             args.err)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            ptx::tmem_ld_32x32b_x32(tO + 32 * c, o);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            ptx::tmem_st_32x32b_x32(tO + 32 * c, o);
+          }
+        }
+        const uint32_t tP = tmem + lane_off + C::col_p(i, j % PB);
+#pragma unroll
+        for (int c = 0; c < BN / 64; ++c)
+          ptx::tmem_st_32x32b_x32(tP + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&pk[32 * c]));
+        ptx::tmem_wait_st();
+        warp_arrive(bar_p_full(j), lane);
       }
-      ptx::tmem_wait_st();
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(p_full(i));
     }
 
     // ------------------------------------------------------------ epilogue
-    if (ok) ok = warp_wait_bar(o_full(i), 0, abort_flag, args.err);
+    if (ok) ok = warp_wait_bar(bar(C::kBarOFull + i), 0, abort_flag, args.err);
     uint32_t all_ok;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t"
@@ -601,8 +740,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           zero_row = mrow[static_cast<int64_t>(row) * args.mask_ss] == 0;
       }
       // a row that saw no visible key is NaN, as torch.softmax of all -inf
-      const float inv_l = zero_row ? 0.f : (m_run == -INFINITY ? __int_as_float(0x7fc00000) : 1.f / l_run);
-      const uint32_t stage = sbase + C::kOffQ + i * C::kTileBytes;  // Q_i is no longer read
+      const float inv_l =
+          zero_row ? 0.f : (m_run == -INFINITY ? __int_as_float(0x7fc00000) : 1.f / l_run);
+      const uint32_t stage = sbase + C::kOffQ + i * C::kQTileBytes;  // Q_i is no longer read
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
@@ -618,10 +758,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (zero_row) a = bb = 0.f;
             w[e] = pack2<kBF16>(a, bb);
           }
-          const int col = 32 * c + 8 * u;           // first element of this 16-byte chunk
-          const int cb = col >> 6;                  // 64-column block
-          const int lc = (col & 63) >> 3;           // logical 16-byte chunk within the row
-          const uint32_t addr = stage + cb * C::kChunkBytes + rl * 128 + ((lc ^ (rl & 7)) << 4);
+          const int col = 32 * c + 8 * u;  // first element of this 16-byte chunk
+          const int cb = col >> 6;         // 64-column block
+          const int lc = (col & 63) >> 3;  // logical 16-byte chunk within the row
+          const uint32_t addr = stage + cb * C::kQChunkBytes + rl * 128 + ((lc ^ (rl & 7)) << 4);
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[0]),
                        "r"(w[1]), "r"(w[2]), "r"(w[3])
                        : "memory");
@@ -629,10 +769,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ptx::fence_proxy_async_smem();
       ptx::named_barrier_sync(1 + i, kBlockM);
-      if (rl == 0 && q0 + kBlockM * i < S) {
+      if (rl == 0 && qstart < S) {
 #pragma unroll
         for (int cb = 0; cb < C::kChunks; ++cb)
-          ptx::tma_store_4d(&tm_o, stage + cb * C::kChunkBytes, 64 * cb, q0 + kBlockM * i, h, b);
+          ptx::tma_store_4d(&tm_o, stage + cb * C::kQChunkBytes, 64 * cb, qstart, h, b);
         ptx::bulk_commit_group();
         ptx::bulk_wait_group_all();
       }
@@ -641,11 +781,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kQkWarp) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);
   }
 }
+
+// Instances: 128-key tiles and one P buffer per query tile; D = 128 shares
+// one S buffer between the query tiles (both fill the 512 TMEM columns).
+using Cfg128 = Cfg<128, 128, 1, 5, true>;
+using Cfg64 = Cfg<64, 128, 1, 10, false>;
 
 // ------------------------------------------------------------------- host
 namespace {
@@ -685,8 +830,9 @@ bool tensor_aligned(const void* ptr, const int64_t st[3], const b200_attn_fwd_pa
   return true;
 }
 
+// 4-D tensor map {D, S, H, B} with a {64, box_rows, 1, 1} box, 128-byte swizzle.
 int encode_map(CUtensorMap* m, const void* ptr, const int64_t st[3],
-               const b200_attn_fwd_params* p) {
+               const b200_attn_fwd_params* p, uint32_t box_rows) {
   auto fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled entry point unavailable");
@@ -695,17 +841,18 @@ int encode_map(CUtensorMap* m, const void* ptr, const int64_t st[3],
   const int64_t D = p->head_dim, S = p->seq_len, H = p->heads, B = p->batch;
   // Size-1 dimensions never move the address; give them a legal stride.
   const int64_t fill = D * 2 * 16;
-  int64_t s_seq = S > 1 ? st[2] * 2 : fill;
-  int64_t s_head = H > 1 ? st[1] * 2 : fill;
-  int64_t s_batch = B > 1 ? st[0] * 2 : fill;
+  const int64_t s_seq = S > 1 ? st[2] * 2 : fill;
+  const int64_t s_head = H > 1 ? st[1] * 2 : fill;
+  const int64_t s_batch = B > 1 ? st[0] * 2 : fill;
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S),
                         static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(B)};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_seq), static_cast<cuuint64_t>(s_head),
                            static_cast<cuuint64_t>(s_batch)};
-  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(kBlockM), 1, 1};
+  cuuint32_t box[4] = {64, box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUtensorMapDataType dt =
-      p->dtype == B200_ATTN_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType dt = p->dtype == B200_ATTN_DTYPE_BF16
+                                     ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = fn(m, dt, 4, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -724,10 +871,9 @@ struct DeviceState {
 };
 DeviceState g_dev[kMaxDevices];
 
-template <int D, int NSLOT, bool C, bool M, bool BF>
+template <class Cf, bool Ca, bool M, bool BF>
 int launch_one(const CUtensorMap maps[4], const KernelArgs& args, int device, cudaStream_t stream) {
-  using Cf = Cfg<D, NSLOT>;
-  auto kernel = attn_fwd_sm100_kernel<D, NSLOT, C, M, BF>;
+  auto kernel = attn_fwd_sm100_kernel<Cf, Ca, M, BF>;
   static std::once_flag attr_once[kMaxDevices];
   static cudaError_t attr_err[kMaxDevices];
   std::call_once(attr_once[device], [&] {
@@ -748,20 +894,20 @@ int launch_one(const CUtensorMap maps[4], const KernelArgs& args, int device, cu
   return B200_ATTN_OK;
 }
 
-template <int D, int NSLOT>
+template <class Cf>
 int dispatch_flags(const CUtensorMap maps[4], const KernelArgs& a, const b200_attn_fwd_params* p,
                    int dev, cudaStream_t s) {
   const bool c = p->causal != 0, m = p->key_mask != nullptr, bf = p->dtype == B200_ATTN_DTYPE_BF16;
   if (c) {
-    if (m) return bf ? launch_one<D, NSLOT, true, true, true>(maps, a, dev, s)
-                     : launch_one<D, NSLOT, true, true, false>(maps, a, dev, s);
-    return bf ? launch_one<D, NSLOT, true, false, true>(maps, a, dev, s)
-              : launch_one<D, NSLOT, true, false, false>(maps, a, dev, s);
+    if (m) return bf ? launch_one<Cf, true, true, true>(maps, a, dev, s)
+                     : launch_one<Cf, true, true, false>(maps, a, dev, s);
+    return bf ? launch_one<Cf, true, false, true>(maps, a, dev, s)
+              : launch_one<Cf, true, false, false>(maps, a, dev, s);
   }
-  if (m) return bf ? launch_one<D, NSLOT, false, true, true>(maps, a, dev, s)
-                   : launch_one<D, NSLOT, false, true, false>(maps, a, dev, s);
-  return bf ? launch_one<D, NSLOT, false, false, true>(maps, a, dev, s)
-            : launch_one<D, NSLOT, false, false, false>(maps, a, dev, s);
+  if (m) return bf ? launch_one<Cf, false, true, true>(maps, a, dev, s)
+                   : launch_one<Cf, false, true, false>(maps, a, dev, s);
+  return bf ? launch_one<Cf, false, false, true>(maps, a, dev, s)
+            : launch_one<Cf, false, false, false>(maps, a, dev, s);
 }
 
 }  // namespace
@@ -847,11 +993,13 @@ extern "C" int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream) {
     return B200_ATTN_ERR_DEVICE;
   }
 
+  const uint32_t kv_rows = p->head_dim == 128 ? Cfg128::BN : Cfg64::BN;
   CUtensorMap maps[4];
-  const void* ptrs[4] = {p->q, p->k, p->v, p->o};
-  const int64_t* strides[4] = {p->q_stride, p->k_stride, p->v_stride, p->o_stride};
-  for (int t = 0; t < 4; ++t)
-    if ((rc = encode_map(&maps[t], ptrs[t], strides[t], p)) != B200_ATTN_OK) return rc;
+  if ((rc = encode_map(&maps[0], p->q, p->q_stride, p, kBlockM)) != B200_ATTN_OK ||
+      (rc = encode_map(&maps[1], p->k, p->k_stride, p, kv_rows)) != B200_ATTN_OK ||
+      (rc = encode_map(&maps[2], p->v, p->v_stride, p, kv_rows)) != B200_ATTN_OK ||
+      (rc = encode_map(&maps[3], p->o, p->o_stride, p, kBlockM)) != B200_ATTN_OK)
+    return rc;
 
   KernelArgs a;
   a.seq_len = static_cast<int32_t>(p->seq_len);
@@ -873,6 +1021,6 @@ extern "C" int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream) {
     return B200_ATTN_ERR_INVALID_ARGUMENT;
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (p->head_dim == 128) return dispatch_flags<128, 4>(maps, a, p, dev, s);
-  return dispatch_flags<64, 6>(maps, a, p, dev, s);
+  if (p->head_dim == 128) return dispatch_flags<Cfg128>(maps, a, p, dev, s);
+  return dispatch_flags<Cfg64>(maps, a, p, dev, s);
 }
