@@ -1,0 +1,80 @@
+"""Module adapter on the GPU: SM100_FUSED is planned and runs the native kernel.
+
+Mirrors the reference's fake-fallback detector (test/test_triton_fused_attention.py:124-138):
+torch.matmul is patched to raise, so a silent fallback to dense PyTorch fails
+the test.  Values are compared with the organiser's operation order.
+"""
+
+from unittest import mock
+
+import pytest
+import torch
+import torch.nn as nn
+
+from b200_attention.attention_dispatch import AttentionMode, AttentionModelSpec
+from b200_attention.modules import B200FusedSelfAttention
+from oracle.reference_attention import reference_attention
+from parity import assert_close
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _baseline(mod, x, mask, causal):
+    B, S, d = x.shape
+    H = mod.num_heads
+    heads = lambda t: t.view(B, S, H, d // H).transpose(1, 2).contiguous().cpu()
+    ctx = reference_attention(heads(mod.q_proj(x)), heads(mod.k_proj(x)), heads(mod.v_proj(x)),
+                              None if mask is None else mask.cpu(), causal, (d // H) ** -0.5)
+    out = mod.out_proj(ctx.to(DEV).transpose(1, 2).contiguous().view(B, S, d))
+    if mask is not None:
+        out = out.masked_fill(~mask[..., None], 0)
+    return out
+
+
+@pytest.mark.parametrize("d_model,heads", [(1024, 16), (1024, 8)])
+def test_module_uses_sm100_kernel(d_model, heads):
+    torch.manual_seed(1)
+    B, S = 2, 300
+    spec = AttentionModelSpec(B, S, d_model, heads, 4 * d_model, 1, True)
+    mod = B200FusedSelfAttention(d_model, heads, model_spec=spec, layer_index=0).to(DEV, torch.bfloat16).eval()
+    for p in mod.parameters():
+        nn.init.normal_(p, std=0.02)
+    x = torch.randn(B, S, d_model, device=DEV, dtype=torch.bfloat16)
+    mask = torch.arange(S, device=DEV)[None, :] < torch.tensor([300, 170], device=DEV)[:, None]
+    with torch.inference_mode():
+        _, plan = mod._attention_plan(x, True, False)
+        assert plan.mode == AttentionMode.SM100_FUSED
+        with mock.patch("torch.matmul", side_effect=AssertionError("dense fallback")):
+            out = mod(x, mask, causal=True)
+        torch.cuda.synchronize()
+        ref = _baseline(mod, x, mask, True)
+    assert_close(out, ref, "module")
+
+
+def test_stacked_blocks_match_baseline_order():
+    """Two pre-LN blocks (the organiser's block, torch_transformer_benchmark.py:126-146)."""
+    torch.manual_seed(2)
+    B, S, d, H = 2, 512, 256, 4
+    spec = AttentionModelSpec(B, S, d, H, 4 * d, 2, True)
+    layers = []
+    for i in range(2):
+        blk = nn.ModuleDict(dict(norm1=nn.LayerNorm(d), norm2=nn.LayerNorm(d),
+                                 attention=B200FusedSelfAttention(d, H, model_spec=spec, layer_index=i),
+                                 ffn_in=nn.Linear(d, 4 * d), ffn_out=nn.Linear(4 * d, d)))
+        layers.append(blk.to(DEV, torch.bfloat16).eval())
+    x0 = torch.randn(B, S, d, device=DEV, dtype=torch.bfloat16)
+    mask = torch.ones(B, S, dtype=torch.bool, device=DEV)
+
+    def run(attn):
+        x = x0
+        for blk in layers:
+            x = x + attn(blk["attention"], blk["norm1"](x))
+            x = x + blk["ffn_out"](torch.nn.functional.gelu(blk["ffn_in"](blk["norm2"](x))))
+        return x
+
+    with torch.inference_mode():
+        fused = run(lambda m, h: m(h, mask, True))
+        ref = run(lambda m, h: _baseline(m, h, mask, True))
+    diff = (fused.float() - ref.float()).abs()
+    assert float(diff.mean()) < 2e-2 and float(diff.max()) < 0.25
