@@ -63,12 +63,28 @@ constexpr float kLog2e = 1.4426950408889634f;
 #endif
 // Of every 8 probabilities, this many are computed with the FMA-pipe exp2.
 constexpr int kPolyPer8 = B200_ATTN_POLY_PER8;
+#ifndef B200_ATTN_F32X2
+#define B200_ATTN_F32X2 1
+#endif
+#ifndef B200_ATTN_SPLIT_LD
+#define B200_ATTN_SPLIT_LD 1
+#endif
+#ifndef B200_ATTN_GROUP_MB
+#define B200_ATTN_GROUP_MB 48
+#endif
+// Packed fp32x2 FMA/ADD in the softmax (same rounding, half the instructions).
+constexpr bool kF32x2 = B200_ATTN_F32X2 != 0;
+// Row max of the first 64 score columns overlaps the TMEM load of the rest.
+constexpr bool kSplitLoad = B200_ATTN_SPLIT_LD != 0;
+// CTAs of heads whose K and V fit in this many MB of L2 run together.
+constexpr int64_t kGroupBytes = static_cast<int64_t>(B200_ATTN_GROUP_MB) << 20;
 
 struct KernelArgs {
   int32_t seq_len;
   int32_t heads;
   int32_t batch;
   int32_t num_q_blocks;  // ceil(S / 256)
+  int32_t group_heads;   // (batch, head) pairs per L2 group of CTAs
   float scale;           // softmax scale
   float scale_log2;      // scale * log2(e)
   int32_t zero_masked_queries;
@@ -150,6 +166,25 @@ __device__ __forceinline__ float round_to_input(float x) {
   }
 }
 
+// Packed fp32x2 a*b+c and a+b (sm_100 fma/add .f32x2): two lanes per
+// instruction, each rounded exactly like the scalar operation.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0,
+                                      float b1, float c0, float c1) {
+  asm("{\n\t.reg .b64 a, b, c, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+      "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0,
+                                      float b1) {
+  asm("{\n\t.reg .b64 a, b, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // Three-input maximum (sm_100 max.f32 with three sources).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
@@ -171,26 +206,32 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
 }
 
-// Max of N consecutive values (N a multiple of 32) as a 3-input tree.
-template <int N>
-__device__ __forceinline__ float row_max(const uint32_t (&s)[N]) {
-  static_assert(N % 32 == 0, "chunks of 32");
-  float cm[N / 32];
+// Max of s[OFF, OFF + CNT) (CNT a multiple of 32) as a 3-input tree.
+template <int OFF, int CNT, int N>
+__device__ __forceinline__ float range_max(const uint32_t (&s)[N]) {
+  static_assert(CNT % 32 == 0 && OFF % 32 == 0 && OFF + CNT <= N, "chunks of 32");
+  float cm[CNT / 32];
 #pragma unroll
-  for (int c = 0; c < N / 32; ++c) {
+  for (int cc = 0; cc < CNT / 32; ++cc) {
+    const int c = OFF / 32 + cc;
     float v[11];
 #pragma unroll
     for (int t = 0; t < 10; ++t)
       v[t] = fmax3(__uint_as_float(s[32 * c + 3 * t]), __uint_as_float(s[32 * c + 3 * t + 1]),
                    __uint_as_float(s[32 * c + 3 * t + 2]));
     v[10] = fmaxf(__uint_as_float(s[32 * c + 30]), __uint_as_float(s[32 * c + 31]));
-    cm[c] = fmax3(fmax3(v[0], v[1], v[2]), fmax3(v[3], v[4], v[5]),
-                  fmax3(v[6], v[7], fmax3(v[8], v[9], v[10])));
+    cm[cc] = fmax3(fmax3(v[0], v[1], v[2]), fmax3(v[3], v[4], v[5]),
+                   fmax3(v[6], v[7], fmax3(v[8], v[9], v[10])));
   }
   float m = cm[0];
 #pragma unroll
-  for (int c = 1; c < N / 32; ++c) m = fmaxf(m, cm[c]);
+  for (int c = 1; c < CNT / 32; ++c) m = fmaxf(m, cm[c]);
   return m;
+}
+
+template <int N>
+__device__ __forceinline__ float row_max(const uint32_t (&s)[N]) {
+  return range_max<0, N, N>(s);
 }
 
 __device__ __forceinline__ int warp_max_i(int v) {
@@ -307,10 +348,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int S = args.seq_len;
 
-  // Heaviest query blocks (causal) are launched first across all heads.
+  // CTAs run in groups of group_heads (batch, head) pairs whose K and V fit
+  // in L2, so the query blocks of a head re-read K/V from L2 rather than HBM;
+  // inside a group the heaviest query blocks (causal) are launched first.
   const int bh_count = args.batch * args.heads;
-  const int qb = args.num_q_blocks - 1 - static_cast<int>(blockIdx.x) / bh_count;
-  const int bh = static_cast<int>(blockIdx.x) % bh_count;
+  const int per_group = args.group_heads * args.num_q_blocks;
+  const int grp = static_cast<int>(blockIdx.x) / per_group;
+  const int rem = static_cast<int>(blockIdx.x) - grp * per_group;
+  const int gsize = min(args.group_heads, bh_count - grp * args.group_heads);
+  const int qb = args.num_q_blocks - 1 - rem / gsize;
+  const int bh = grp * args.group_heads + rem % gsize;
   const int b = bh / args.heads;
   const int h = bh % args.heads;
   const int q0 = qb * kRowsPerCta;
@@ -652,12 +699,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::tc_fence_after();
         uint32_t sr[BN];
-        load_row<BN>(tS, sr);
-        warp_arrive(bar_s_free, lane);  // the MMA warp may now overwrite S_i
+        float mx;
+        if (partial_tile(j, mw)) {
+          load_row<BN>(tS, sr);
+          warp_arrive(bar_s_free, lane);  // the MMA warp may now overwrite S_i
+          mask_row<BN>(sr, visible_limit(j), mw);
+          mx = row_max<BN>(sr);
+        } else if constexpr (kSplitLoad && BN == 128) {
+          // max of columns [0,64) while columns [64,128) are still in flight
+          ptx::tmem_ld_32x32b_x32(tS, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+          ptx::tmem_ld_32x32b_x32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+          ptx::tmem_wait_ld();
+          ptx::tmem_ld_32x32b_x32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+          ptx::tmem_ld_32x32b_x32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+          const float m_lo = range_max<0, 64, BN>(sr);
+          ptx::tmem_wait_ld();
+          warp_arrive(bar_s_free, lane);
+          mx = fmaxf(m_lo, range_max<64, 64, BN>(sr));
+        } else {
+          load_row<BN>(tS, sr);
+          warp_arrive(bar_s_free, lane);
+          mx = row_max<BN>(sr);
+        }
 
-        if (partial_tile(j, mw)) mask_row<BN>(sr, visible_limit(j), mw);
-
-        const float m_cand = row_max<BN>(sr) * scale_log2;
+        const float m_cand = mx * scale_log2;
         const bool resc = m_cand > m_run + kRescaleLog2;
         const float m_new = resc ? m_cand : m_run;
         const float alpha = resc ? ptx::ex2_approx(m_run - m_new) : 1.f;
@@ -671,14 +736,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[BN / 2];
 #pragma unroll
         for (int e = 0; e < BN / 2; ++e) {
-          float p2[2];
+          float x[2], p2[2];
+          if constexpr (kF32x2) {
+            ffma2(x[0], x[1], __uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1]),
+                  scale_log2, scale_log2, neg_m, neg_m);
+          } else {
+            x[0] = fmaf(__uint_as_float(sr[2 * e]), scale_log2, neg_m);
+            x[1] = fmaf(__uint_as_float(sr[2 * e + 1]), scale_log2, neg_m);
+          }
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             const int k = 2 * e + hh;
-            const float x = fmaf(__uint_as_float(sr[k]), scale_log2, neg_m);
-            p2[hh] = ((k & 7) < kPolyPer8) ? ex2_poly(fmaxf(x, -126.f)) : ptx::ex2_approx(x);
+            p2[hh] = ((k & 7) < kPolyPer8) ? ex2_poly(fmaxf(x[hh], -126.f))
+                                           : ptx::ex2_approx(x[hh]);
           }
-          sum[e & 3] += p2[0] + p2[1];
+          if constexpr (kF32x2) {
+            const int a = 2 * (e & 1);
+            fadd2(sum[a], sum[a + 1], sum[a], sum[a + 1], p2[0], p2[1]);
+          } else {
+            sum[e & 3] += p2[0] + p2[1];
+          }
           pk[e] = pack2<kBF16>(p2[0], p2[1]);
         }
         l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
@@ -1006,6 +1083,12 @@ extern "C" int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream) {
   a.heads = static_cast<int32_t>(p->heads);
   a.batch = static_cast<int32_t>(p->batch);
   a.num_q_blocks = static_cast<int32_t>((p->seq_len + kRowsPerCta - 1) / kRowsPerCta);
+  {
+    const int64_t bh = p->batch * p->heads;
+    const int64_t kv_bytes = 4 * p->seq_len * p->head_dim;  // K and V of one head, 16-bit
+    int64_t g = kGroupBytes > 0 ? kGroupBytes / kv_bytes : bh;
+    a.group_heads = static_cast<int32_t>(g < 1 ? 1 : (g > bh ? bh : g));
+  }
   a.scale = p->scale;
   a.scale_log2 = p->scale * kLog2e;
   a.zero_masked_queries = p->zero_masked_queries;
