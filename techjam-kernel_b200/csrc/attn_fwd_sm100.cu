@@ -69,6 +69,15 @@ constexpr int kPolyPer8 = B200_ATTN_POLY_PER8;
 #ifndef B200_ATTN_SPLIT_LD
 #define B200_ATTN_SPLIT_LD 1
 #endif
+#ifndef B200_ATTN_ISSUER_SPIN
+#define B200_ATTN_ISSUER_SPIN 1
+#endif
+// MMA issuers poll their barriers without suspending before the bounded
+// wait: a suspended issuer was measured to resume hundreds of cycles after
+// the softmax signalled, which sits directly on the scores -> softmax chain.
+// (Softmax warps keep suspending waits: their polling would take issue slots
+// from the other softmax warpgroup on the same SM sub-partition.)
+constexpr int kIssuerSpin = B200_ATTN_ISSUER_SPIN ? 4096 : 0;
 #ifndef B200_ATTN_GROUP_MB
 #define B200_ATTN_GROUP_MB 48
 #endif
@@ -262,6 +271,16 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity,
                                          volatile uint32_t* abort_flag, int32_t* err) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
   return wait_bar_slow(bar, parity, abort_flag, err);
+}
+
+// Issuer-side wait: poll without suspending first (a suspended thread resumes
+// late), then the bounded wait.
+__device__ __forceinline__ bool issuer_wait(uint32_t bar, uint32_t parity,
+                                            volatile uint32_t* abort_flag, int32_t* err) {
+#pragma unroll 1
+  for (int k = 0; k < kIssuerSpin; ++k)
+    if (ptx::mbar_test_wait(bar, parity)) return true;
+  return wait_bar(bar, parity, abort_flag, err);
 }
 
 // Wait by every lane of a warp; the result is made warp-uniform so the
@@ -500,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok || j >= n_tiles[i]) continue;
           const int sb = C::kSharedS ? 0 : i;
           if (prev_i[sb] >= 0 &&
-              !wait_bar(bar(C::kBarSFree + prev_i[sb]), prev_j[sb] & 1, abort_flag, args.err)) {
+              !issuer_wait(bar(C::kBarSFree + prev_i[sb]), prev_j[sb] & 1, abort_flag, args.err)) {
             ok = false;
             break;
           }
@@ -543,8 +562,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           if (!ok || j >= n_tiles[i]) continue;
-          if (!wait_bar(bar(C::kBarPFull + i * PB + (j % PB)), (j / PB) & 1, abort_flag,
-                        args.err)) {
+          if (!issuer_wait(bar(C::kBarPFull + i * PB + (j % PB)), (j / PB) & 1, abort_flag,
+                           args.err)) {
             ok = false;
             break;
           }
