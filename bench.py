@@ -3,6 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg2]
     python bench.py --impl reference ...      # reference's CPU attention path
+    python bench.py --impl torch-dense ...    # yardstick: the reference's dense path on this GPU
 
 A step is one attention forward over one batch of the workload (one kernel
 launch).  ``value`` is whole-job TFLOP/s with inputs resident in HBM; ``e2e``
@@ -237,13 +238,87 @@ def run_reference_arm(args, cfg: dict, rank: int, world: int) -> int:
     return 0
 
 
+def dense_torch_attention(q, k, v, mask, causal: bool, scale: float, max_score_bytes: int):
+    """The reference's own B200 path in torch CUDA ops: _reference_attention
+    (model/triton_fused_attention.py:1256-1285), which the reference's planner
+    selects on capability 10.x (model/attention_dispatch.py:362-363).  QK^T in
+    the input dtype, x scale in dtype, causal triu(1) and key mask to -inf, fp32
+    softmax, cast, PV.  Heads are processed in chunks so the fp32 score tensor
+    stays under max_score_bytes.  Returns [B, H, S, D]."""
+    import torch
+
+    B, H, S, D = q.shape
+    out = torch.empty_like(q)
+    per_head = S * S * 4
+    hc = max(1, min(H, max_score_bytes // per_head))
+    tri = torch.ones((S, S), dtype=torch.bool, device=q.device).triu(1) if causal else None
+    for b in range(B):
+        for h0 in range(0, H, hc):
+            h1 = min(H, h0 + hc)
+            s = torch.matmul(q[b, h0:h1], k[b, h0:h1].transpose(-1, -2)) * scale
+            if tri is not None:
+                s = s.masked_fill(tri, float("-inf"))
+            if mask is not None:
+                s = s.masked_fill(~mask[b][None, None, :], float("-inf"))
+            p = torch.softmax(s.float(), dim=-1).to(q.dtype)
+            out[b, h0:h1] = torch.matmul(p, v[b, h0:h1])
+    return out
+
+
+def run_dense_arm(args, cfg: dict, rank: int, world: int) -> int:
+    """Yardstick (not the reference arm): the reference's dense PyTorch attention
+    run on this GPU, the path a B200 takes today without this kernel."""
+    if rank != 0:
+        return 0
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, H, _ = shard_for(cfg, 1, 0)
+    S, D, causal = cfg["S"], cfg["D"], cfg["causal"]
+    lengths = valid_lengths(cfg, args.seed)
+    flop = flops_for(cfg, B, H, lengths)
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    q, k, v = (torch.randn((B, H, S, D), generator=gen, device=dev).to(torch.bfloat16)
+               for _ in range(3))
+    mask = None
+    if lengths is not None:
+        mask = torch.arange(S, device=dev)[None, :] < torch.tensor(lengths, device=dev)[:, None]
+    cap = 16 * 2 ** 30
+    for _ in range(args.warmup):
+        dense_torch_attention(q, k, v, mask, causal, D ** -0.5, cap)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(0)
+    stream = torch.cuda.current_stream(dev)
+    with sampler:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            dense_torch_attention(q, k, v, mask, causal, D ** -0.5, cap)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    line = {
+        "impl": "torch-dense", "metric": METRIC, "value": flop / (ms * 1e-3) / 1e12, "unit": UNIT,
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded torch.randn N(0,1))",
+        "config": {"workload": args.workload, **{k: cfg[k] for k in ("B", "H", "S", "D", "causal")},
+                   "per_gpu_batch_heads": [B, H],
+                   "impl_path": "dense torch CUDA ops in _reference_attention's order (cuBLAS GEMMs)"},
+        "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9,
+        "clocks": sampler.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS))
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "torch-dense"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -259,6 +334,8 @@ def main(argv=None) -> int:
 
     if args.impl == "reference":
         return run_reference_arm(args, cfg, rank, world)
+    if args.impl == "torch-dense":
+        return run_dense_arm(args, cfg, rank, world)
 
     import torch
     import torch.distributed as dist
