@@ -870,7 +870,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cb = 0; cb < C::kChunks; ++cb)
           ptx::tma_store_4d(&tm_o, stage + cb * C::kQChunkBytes, 64 * cb, qstart, h, b);
         ptx::bulk_commit_group();
-        ptx::bulk_wait_group_all();
+        ptx::bulk_wait_group_read_all();  // shared memory may go once the store has read it
       }
     }
   }

@@ -108,6 +108,12 @@ __device__ __forceinline__ void bulk_wait_group_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// Waits until every committed bulk store has finished READING its shared
+// memory source (the global writes may still be in flight).
+__device__ __forceinline__ void bulk_wait_group_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 // ------------------------------------------------------------------ tcgen05
 // TMEM allocation: executed by one full warp; the allocated column base is
 // written to shared memory at `dst`.
