@@ -47,6 +47,10 @@ WORKLOADS = {
     "cfg3": dict(B=16, H=32, S=4096, D=128, causal=False, masked=True, shard="batch"),
     "cfg4": dict(B=1, H=32, S=32768, D=128, causal=True, masked=False, shard="heads"),
     "ns": dict(B=8, H=16, S=8192, D=128, causal=True, masked=False, shard="batch"),
+    # end-to-end: 12-layer pre-LN decoder, d_model 1024, FFN 4096, vocab 32000;
+    # global batch 8 split over the ranks (data parallel)
+    "cfg5": dict(B=8, H=16, S=2048, D=64, causal=True, masked=False, shard="batch_split",
+                 layers=12, d_model=1024, ffn=4096, vocab=32000),
 }
 
 
@@ -87,6 +91,9 @@ def shard_for(cfg: dict, world: int, rank: int) -> tuple[int, int, str]:
         lo = (H * rank) // world
         hi = (H * (rank + 1)) // world
         return cfg["B"], hi - lo, "strong"
+    if cfg["shard"] == "batch_split":
+        B = cfg["B"]
+        return (B * (rank + 1)) // world - (B * rank) // world, cfg["H"], "strong"
     return cfg["B"], cfg["H"], "weak"
 
 
@@ -312,6 +319,131 @@ def run_dense_arm(args, cfg: dict, rank: int, world: int) -> int:
     return 0
 
 
+def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, barrier,
+                  max_over_ranks) -> int:
+    """cfg5: forward of the 12-layer decoder whose attention is the sm_100a kernel.
+
+    A step is one forward over this rank's share of the global batch of 8
+    sequences (token ids -> embedding -> 12 blocks -> final LayerNorm).  value
+    = whole-job decoder TFLOP/s (projections, FFN and causal attention).  The
+    attention kernel alone is timed at the same per-rank shape for the
+    roofline and the attention share of the forward."""
+    import torch
+    import torch.distributed as dist
+
+    from b200_attention.fused_attention import b200_fused_attention, read_device_errors
+    from b200_attention.transformer import Decoder, DecoderConfig, init_normal_
+
+    B, H, scaling = shard_for(cfg, world, rank)
+    S, D = cfg["S"], cfg["D"]
+    dcfg = DecoderConfig(B, S, cfg["d_model"], H, cfg["ffn"], cfg["layers"], cfg["causal"],
+                         vocab_size=cfg["vocab"])
+    model = init_normal_(Decoder(dcfg), seed=args.seed).to(device=dev, dtype=torch.bfloat16).eval()
+    flop_rank = dcfg.forward_flops()
+    tot = torch.tensor([flop_rank], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tot)
+    flop_job = float(tot.item())
+    gen = torch.Generator(device="cpu").manual_seed(args.seed + 1000 * rank)
+    n_sets = 2
+    tokens = [torch.randint(0, cfg["vocab"], (B, S), generator=gen).to(dev) for _ in range(n_sets)]
+    stream = torch.cuda.current_stream(dev)
+
+    with torch.inference_mode():
+        for i in range(max(args.warmup, 3)):
+            model(tokens[i % n_sets])
+        torch.cuda.synchronize(dev)
+        if read_device_errors(dev):
+            raise RuntimeError("kernel reported a device error during warm-up")
+        sampler = ClockSampler(local_rank)
+        barrier()
+        torch.cuda.synchronize(dev)
+        with sampler:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(args.steps):
+                out = model(tokens[i % n_sets])
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        barrier()
+        ms_per_step = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+        value = flop_job / (ms_per_step * 1e-3) / 1e12
+        finite = bool(torch.isfinite(out.float()).all())
+
+        # the attention kernel alone at this rank's shape (per-launch events)
+        g2 = torch.Generator(device=dev).manual_seed(args.seed)
+        q, k, v = (torch.randn((B, H, S, D), generator=g2, device=dev).to(torch.bfloat16)
+                   for _ in range(3))
+        for _ in range(3):
+            b200_fused_attention(q, k, v, None, True)
+        torch.cuda.synchronize(dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(20)]
+        for a, b in ev:
+            a.record(stream)
+            b200_fused_attention(q, k, v, None, True)
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        attn_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+        attn_flop = 4.0 * B * H * S * S * D / 2
+        errors = read_device_errors(dev)
+
+        # end to end: token ids from pinned host memory, output back to the host
+        htok = tokens[0].cpu().pin_memory()
+        hout = torch.empty((B, S, cfg["d_model"]), dtype=torch.bfloat16).pin_memory()
+        for _ in range(2):
+            hout.copy_(model(htok.to(dev, non_blocking=True)), non_blocking=True)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            hout.copy_(model(htok.to(dev, non_blocking=True)), non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = CpuReference(cfg, args.seed).measure(args.cpu_budget, min_reps=3)
+    peaks, peak_src = load_peaks()
+    peak = peaks["bf16_tflops"]
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    attn_tflops = attn_flop / (attn_ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s (decoder forward)", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform random token ids, random-init weights N(0, 0.02))",
+        "config": {"workload": "cfg5", "layers": cfg["layers"], "d_model": cfg["d_model"],
+                   "heads": H, "head_dim": D, "ffn": cfg["ffn"], "vocab": cfg["vocab"],
+                   "global_batch": cfg["B"], "per_rank_batch": B, "seq_len": S, "causal": True,
+                   "parallelism": f"data-parallel batch split x{world}, no data-path collective",
+                   "l2": f"{n_sets} token sets; each forward streams ~0.4 GB of weights and activations (> L2)",
+                   "flop_per_step_job": flop_job},
+        "attention": {"tflops": attn_tflops, "ms_per_layer": attn_ms,
+                      "share_of_forward": cfg["layers"] * attn_ms / ms_per_step},
+        "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": peak, "unit": "TFLOP/s",
+                     "frac": attn_tflops / peak, "traffic": None,
+                     "kernel": "attn_fwd_sm100_kernel at the per-rank attention shape",
+                     "peak_source": f"{peak_src} bf16_tflops (burst, kernel timed alone)"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": flop_rank / (e2e_ms * 1e-3) / 1e12 * world, "unit": "TFLOP/s (decoder forward)",
+                "h2d_bytes_per_step": htok.numel() * htok.element_size(),
+                "d2h_bytes_per_step": hout.numel() * hout.element_size(), "ms_per_step": e2e_ms},
+        "gpu_launches": args.steps * cfg["layers"],
+        "clocks": sampler.summary(),
+        "validation": {"finite": finite, "device_errors": errors},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -362,6 +494,9 @@ def main(argv=None) -> int:
         t = torch.tensor([x], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    if args.workload == "cfg5":
+        return run_model_arm(args, cfg, rank, world, local_rank, dev, barrier, max_over_ranks)
 
     B, H, scaling = shard_for(cfg, world, rank)
     S, D, causal = cfg["S"], cfg["D"], cfg["causal"]
