@@ -8,10 +8,13 @@ plan cache keyed by dtype, device, shape, causality and autograd (:2216-2285).
 
 Per layer the planner picks the executor:
 
-* ``SM100_FUSED``: q/k/v stay transposed views of the projections (no copies,
-  reference :2287-2292); the sm_100a kernel writes the context directly in the
-  [B, S, H, D] layout ``out_proj`` consumes; padded query rows are zeroed after
-  ``out_proj`` exactly as the reference does (:2456-2461).
+* ``SM100_FUSED``: one GEMM computes Q, K and V together against the three
+  projection weights stacked ([3d, d], cached until a weight changes); q/k/v
+  are strided head views of its [B, S, 3, H, D] output (no copies; the
+  reference keeps per-projection views, :2287-2292); the sm_100a kernel writes
+  the context directly in the [B, S, H, D] layout ``out_proj`` consumes;
+  padded query rows are zeroed after ``out_proj`` exactly as the reference
+  does (:2456-2461).
 * ``EXACT_REFERENCE`` / ``FP32_BASELINE_EXACT``: the planner routes inputs the
   kernel does not cover (autograd, fp32, other head sizes, non-CUDA devices) to
   the organiser's PyTorch operation order, as the reference planner does.
@@ -68,6 +71,8 @@ class B200FusedSelfAttention(nn.Module):
         self._attention_layer_index = layer_index
         self._plan_key: Optional[tuple] = None
         self._plan_value: Optional[tuple] = None
+        self._qkv_key: Optional[tuple] = None
+        self._qkv_value: Optional[tuple] = None
         self.q_proj = nn.Linear(d_model, d_model, bias=True)
         self.k_proj = nn.Linear(d_model, d_model, bias=True)
         self.v_proj = nn.Linear(d_model, d_model, bias=True)
@@ -104,6 +109,19 @@ class B200FusedSelfAttention(nn.Module):
         return self._plan_value
 
     # ------------------------------------------------------------- forward
+    def _stacked_qkv(self):
+        """[3d, d] weight and [3d] bias of the q, k, v projections, rebuilt
+        only when one of them changed (identity, storage or version)."""
+        params = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight,
+                  self.q_proj.bias, self.k_proj.bias, self.v_proj.bias)
+        key = tuple((id(t), t.data_ptr(), t._version, t.dtype, t.device) for t in params)
+        if self._qkv_key != key:
+            with torch.no_grad():
+                weight = torch.cat(params[:3], dim=0)
+                bias = torch.cat(params[3:], dim=0)
+            self._qkv_key, self._qkv_value = key, (weight, bias)
+        return self._qkv_value
+
     def _heads_view(self, projected: torch.Tensor) -> torch.Tensor:
         batch, seq_len, _ = projected.shape
         return projected.view(batch, seq_len, self.num_heads, self.head_dim).transpose(1, 2)
@@ -116,9 +134,10 @@ class B200FusedSelfAttention(nn.Module):
         _, plan = self._attention_plan(x, causal, needs_autograd)
 
         if plan.mode == AttentionMode.SM100_FUSED:
-            q = self._heads_view(self.q_proj(x))
-            k = self._heads_view(self.k_proj(x))
-            v = self._heads_view(self.v_proj(x))
+            weight, bias = self._stacked_qkv()
+            qkv = torch.nn.functional.linear(x, weight, bias).view(
+                batch, seq_len, 3, self.num_heads, self.head_dim)
+            q, k, v = (qkv[:, :, t].transpose(1, 2) for t in range(3))
             context = b200_fused_attention(q, k, v, valid_token_mask, causal, self.scale,
                                            output_bshd=True)
             context = context.view(batch, seq_len, self.d_model)
