@@ -455,6 +455,8 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--graph", action="store_true",
+                    help="replay the timed steps from a CUDA graph (launch-bound workloads)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -544,6 +546,22 @@ def main(argv=None) -> int:
     # ---- device-resident timed region
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
+    graph = None
+    if args.graph:
+        # the K steps captured once and replayed: no host work inside the timed
+        # region (for launch-bound workloads such as cfg1)
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        with torch.cuda.stream(cap):
+            step(0)
+            cap.synchronize()
+            with torch.cuda.graph(graph, stream=cap):
+                for i in range(args.steps):
+                    step(i)
+        stream.wait_stream(cap)
+        graph.replay()
+        torch.cuda.synchronize(dev)
     sampler = ClockSampler(local_rank)
     barrier()
     torch.cuda.synchronize(dev)
@@ -551,16 +569,21 @@ def main(argv=None) -> int:
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record(stream)
-        for i in range(args.steps):
-            ev[i][0].record(stream)
-            step(i)
-            ev[i][1].record(stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(args.steps):
+                ev[i][0].record(stream)
+                step(i)
+                ev[i][1].record(stream)
         t_end.record(stream)
         torch.cuda.synchronize(dev)
     barrier()
     elapsed_ms = max_over_ranks(t_start.elapsed_time(t_end))
-    launch_ms = [a.elapsed_time(b) for a, b in ev]
-    avg_launch_ms = statistics.mean(launch_ms)
+    if graph is not None:
+        avg_launch_ms = t_start.elapsed_time(t_end) / args.steps  # back-to-back launches
+    else:
+        avg_launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
     errors = read_device_errors(dev)
     ms_per_step = elapsed_ms / args.steps
     value = flop_job / (ms_per_step * 1e-3) / 1e12
@@ -648,6 +671,7 @@ def main(argv=None) -> int:
             "per_rank_batch_heads": [B, H],
             "parallelism": f"{'bxh' if scaling == 'weak' else 'heads'}-shard x{world}, no data-path collective",
             "l2": f"inputs rotated over {n_sets} buffer sets of {bytes_per_set / 2**20:.0f} MiB (> L2)",
+            "launch": "CUDA graph of the timed steps" if graph is not None else "eager, one operator call per step",
             "flop_per_step_job": flop_job,
             "valid_lengths": lengths,
         },

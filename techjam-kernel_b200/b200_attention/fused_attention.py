@@ -84,10 +84,21 @@ def unsupported_reason(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Opt
         return "q/k/v must have a contiguous last dimension"
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
         return "the kernel is inference-only (autograd requested)"
-    major, _ = torch.cuda.get_device_capability(q.device)
+    major = _capability_major(q.device)
     if major != 10:
         return f"the kernel is built for sm_100a; device capability is {major}.x"
     return None
+
+
+_capability: dict = {}
+
+
+def _capability_major(device: torch.device) -> int:
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    major = _capability.get(index)
+    if major is None:
+        major = _capability[index] = torch.cuda.get_device_capability(index)[0]
+    return major
 
 
 def device_error_word(device: torch.device) -> torch.Tensor:

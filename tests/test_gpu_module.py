@@ -14,7 +14,8 @@ import torch.nn as nn
 from b200_attention.attention_dispatch import AttentionMode, AttentionModelSpec
 from b200_attention.modules import B200FusedSelfAttention
 from oracle.reference_attention import reference_attention
-from parity import assert_close
+from b200_attention.fused_attention import b200_fused_attention
+from parity import assert_close, seeded_qkv
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
@@ -78,3 +79,31 @@ def test_stacked_blocks_match_baseline_order():
         ref = run(lambda m, h: _baseline(m, h, mask, True))
     diff = (fused.float() - ref.float()).abs()
     assert float(diff.mean()) < 2e-2 and float(diff.max()) < 0.25
+
+
+@pytest.mark.gpu
+def test_operator_replays_in_a_cuda_graph():
+    """The operator launches on the caller's stream with no allocation (given
+    ``out``) and no host synchronisation, so it can be captured in a CUDA graph;
+    replays must equal eager calls bit for bit."""
+    dev = torch.device("cuda", 0)
+    q, k, v = seeded_qkv((2, 4, 384, 128), torch.bfloat16, 21, device=dev)
+    out = torch.empty((2, 384, 4, 128), device=dev, dtype=torch.bfloat16)
+    eager = b200_fused_attention(q, k, v, None, True, output_bshd=True).clone()
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        b200_fused_attention(q, k, v, None, True, output_bshd=True, out=out)
+        stream.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            b200_fused_attention(q, k, v, None, True, output_bshd=True, out=out)
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    out.zero_()
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    assert torch.equal(out, eager)
+    q.mul_(0.5)  # new inputs in the same buffers: a replay sees them
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    assert torch.equal(out, b200_fused_attention(q, k, v, None, True, output_bshd=True))
