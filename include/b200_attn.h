@@ -114,6 +114,19 @@ B200_ATTN_API int32_t b200_attn_launches_per_call(const b200_attn_fwd_params* p)
  * tensor-map encoding failure); empty when none. */
 B200_ATTN_API const char* b200_attn_last_error_detail(void);
 
+/* Self-test of failure detection (no reference counterpart).  Launches the
+ * forward exactly like b200_attn_fwd, except that in every CTA the K/V load
+ * number `skipped_load` (0 = first K tile, 1 = first V tile, ...) is announced
+ * to its barrier but never issued.  The pipeline wait on it runs out after its
+ * one-second bound: the kernel ORs B200_ATTN_DEVERR_WAIT_TIMEOUT into
+ * *error_word, lets every role fall through, waits (bounded) for its own copies
+ * and MMAs, frees TMEM and returns, leaving the CUDA context usable.  Supported
+ * for bf16, head_dim 128, causal, no mask, with a non-null error_word
+ * (B200_ATTN_ERR_UNSUPPORTED otherwise).  A CTA that reaches the skipped load
+ * takes about two seconds; the output is undefined. */
+B200_ATTN_API int32_t b200_attn_selftest_stall(const b200_attn_fwd_params* p, int32_t skipped_load,
+                                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

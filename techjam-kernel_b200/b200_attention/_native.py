@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "b200_attn_error_string",
     "b200_attn_launches_per_call",
     "b200_attn_last_error_detail",
+    "b200_attn_selftest_stall",
 )
 
 
@@ -96,6 +97,9 @@ def load_library() -> ctypes.CDLL:
         lib.b200_attn_launches_per_call.argtypes = [ctypes.POINTER(FwdParams)]
         lib.b200_attn_last_error_detail.restype = ctypes.c_char_p
         lib.b200_attn_last_error_detail.argtypes = []
+        lib.b200_attn_selftest_stall.restype = ctypes.c_int32
+        lib.b200_attn_selftest_stall.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_int32,
+                                                 ctypes.c_void_p]
         _lib = lib
         return lib
 

@@ -109,7 +109,10 @@ def device_error_word(device: torch.device) -> torch.Tensor:
         with _error_lock:
             word = _error_words.get(index)
             if word is None:
-                word = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+                # a normal tensor even when the first call runs under
+                # torch.inference_mode(), so read_device_errors can clear it anywhere
+                with torch.inference_mode(False):
+                    word = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
                 _error_words[index] = word
     return word
 

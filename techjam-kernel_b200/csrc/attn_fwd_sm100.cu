@@ -103,6 +103,7 @@ struct KernelArgs {
   void* o;               // output base (for zero rows of skipped blocks)
   int64_t o_sb, o_sh, o_ss;  // elements
   int32_t* err;
+  int32_t skip_load;     // stall self-test only: K/V load left out (see b200_attn_selftest_stall)
 };
 
 // Compile-time shape of one kernel instance.
@@ -351,7 +352,10 @@ __device__ __forceinline__ void mask_row(uint32_t (&s)[N], int lim, const uint32
 }
 
 // ----------------------------------------------------------------- kernel
-template <class C, bool kCausal, bool kMask, bool kBF16>
+// kStallProbe (self-test instance only): K/V load number args.skip_load of
+// every CTA is announced to its barrier but never issued, so the pipeline
+// waits on it run out and exercise the abort path.
+template <class C, bool kCausal, bool kMask, bool kBF16, bool kStallProbe = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
@@ -481,6 +485,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           ptx::mbar_arrive_expect_tx(bar(C::kBarSlotFull + s), C::kKVTileBytes);
+          if (kStallProbe && static_cast<int32_t>(L) == args.skip_load) {
+            ++L;  // the announced bytes never arrive
+            continue;
+          }
           const CUtensorMap* tm = kv ? &tm_v : &tm_k;
 #pragma unroll
           for (int c = 0; c < C::kChunks; ++c)
@@ -971,9 +979,9 @@ struct DeviceState {
 };
 DeviceState g_dev[kMaxDevices];
 
-template <class Cf, bool Ca, bool M, bool BF>
+template <class Cf, bool Ca, bool M, bool BF, bool SP = false>
 int launch_one(const CUtensorMap maps[4], const KernelArgs& args, int device, cudaStream_t stream) {
-  auto kernel = attn_fwd_sm100_kernel<Cf, Ca, M, BF>;
+  auto kernel = attn_fwd_sm100_kernel<Cf, Ca, M, BF, SP>;
   static std::once_flag attr_once[kMaxDevices];
   static cudaError_t attr_err[kMaxDevices];
   std::call_once(attr_once[device], [&] {
@@ -1062,7 +1070,12 @@ extern "C" int32_t b200_attn_launches_per_call(const b200_attn_fwd_params* p) {
   return b200_attn_check(p) == B200_ATTN_OK ? 1 : 0;
 }
 
-extern "C" int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream) {
+namespace b200attn {
+namespace {
+
+// Validates p, selects its device and fills the tensor maps and kernel
+// arguments; returns a B200_ATTN_* code.
+int32_t prepare(const b200_attn_fwd_params* p, CUtensorMap maps[4], KernelArgs& a, int& dev_out) {
   int32_t rc = b200_attn_check(p);
   if (rc != B200_ATTN_OK) return rc;
 
@@ -1094,14 +1107,12 @@ extern "C" int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream) {
   }
 
   const uint32_t kv_rows = p->head_dim == 128 ? Cfg128::BN : Cfg64::BN;
-  CUtensorMap maps[4];
   if ((rc = encode_map(&maps[0], p->q, p->q_stride, p, kBlockM)) != B200_ATTN_OK ||
       (rc = encode_map(&maps[1], p->k, p->k_stride, p, kv_rows)) != B200_ATTN_OK ||
       (rc = encode_map(&maps[2], p->v, p->v_stride, p, kv_rows)) != B200_ATTN_OK ||
       (rc = encode_map(&maps[3], p->o, p->o_stride, p, kBlockM)) != B200_ATTN_OK)
     return rc;
 
-  KernelArgs a;
   a.seq_len = static_cast<int32_t>(p->seq_len);
   a.heads = static_cast<int32_t>(p->heads);
   a.batch = static_cast<int32_t>(p->batch);
@@ -1127,10 +1138,38 @@ extern "C" int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream) {
   a.o_sh = p->o_stride[1];
   a.o_ss = p->o_stride[2];
   a.err = p->error_word;
+  a.skip_load = -1;
   if (static_cast<int64_t>(a.num_q_blocks) * p->batch * p->heads > 0x7fffffffll)
     return B200_ATTN_ERR_INVALID_ARGUMENT;
+  dev_out = dev;
+  return B200_ATTN_OK;
+}
 
+}  // namespace
+}  // namespace b200attn
+
+extern "C" int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream) {
+  CUtensorMap maps[4];
+  KernelArgs a;
+  int dev = 0;
+  const int32_t rc = prepare(p, maps, a, dev);
+  if (rc != B200_ATTN_OK) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (p->head_dim == 128) return dispatch_flags<Cfg128>(maps, a, p, dev, s);
   return dispatch_flags<Cfg64>(maps, a, p, dev, s);
+}
+
+extern "C" int32_t b200_attn_selftest_stall(const b200_attn_fwd_params* p, int32_t skipped_load,
+                                             void* stream) {
+  if (!p || p->head_dim != 128 || p->dtype != B200_ATTN_DTYPE_BF16 || !p->causal || p->key_mask ||
+      !p->error_word || skipped_load < 0)
+    return B200_ATTN_ERR_UNSUPPORTED;
+  CUtensorMap maps[4];
+  KernelArgs a;
+  int dev = 0;
+  const int32_t rc = prepare(p, maps, a, dev);
+  if (rc != B200_ATTN_OK) return rc;
+  a.skip_load = skipped_load;
+  return launch_one<Cfg128, true, false, true, true>(maps, a, dev,
+                                                    reinterpret_cast<cudaStream_t>(stream));
 }

@@ -69,3 +69,24 @@ def test_functional_op_rejects_cpu_inputs_loudly():
         b200_fused_attention(q, q.float(), q)
     with pytest.raises(ValueError):
         b200_fused_attention(q, q, q, valid_token_mask=torch.ones(1, 7, dtype=torch.bool))
+
+
+def test_error_word_survives_inference_mode(monkeypatch):
+    """The per-device error word is created as a normal tensor even when the
+    first kernel call happens under torch.inference_mode(), so it can be
+    cleared outside it (CPU stand-in for the CUDA device)."""
+    from b200_attention import fused_attention as fa
+
+    real_zeros = torch.zeros
+
+    def fake_zeros(*args, **kwargs):
+        kwargs["device"] = "cpu"
+        return real_zeros(*args, **kwargs)
+
+    monkeypatch.setattr(fa, "_error_words", {})
+    monkeypatch.setattr(fa.torch, "zeros", fake_zeros)
+    with torch.inference_mode():
+        word = fa.device_error_word(torch.device("cuda", 0))
+    monkeypatch.undo()
+    assert not word.is_inference()
+    word.zero_()
