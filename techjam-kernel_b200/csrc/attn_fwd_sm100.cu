@@ -6,22 +6,26 @@
 // the input dtype, times v.  Fully masked rows give NaN like torch.softmax.
 //
 // Work decomposition.  One CTA owns 256 query rows of one (batch, head) as two
-// 128-row tiles Q0, Q1 and streams BN-key K/V tiles (BN = 64 for D = 128,
-// 128 for D = 64) through a shared-memory ring.  Ten warps, one job each:
+// 128-row tiles Q0, Q1 and streams 128-key K/V tiles through a shared-memory
+// ring.  Eleven warps, one job each:
 //   warps 0-3  softmax for Q0 (one thread per query row = one TMEM lane)
 //   warps 4-7  softmax for Q1
 //   warp  8    TMA producer (Q once, then K_j, V_j into the ring)
-//   warp  9    tcgen05 issuer (one elected thread) and TMEM owner
+//   warp  9    tcgen05 issuer of the QK products (one thread) and TMEM owner
+//   warp 10    tcgen05 issuer of the PV products (one thread)
 // Tensor memory (512 columns x 128 lanes of 32 bit) holds the scores
-// S = Q_i K_j^T (BN fp32 columns), one buffer of P_i per query tile (BN/2
-// columns of packed 16-bit pairs) and the fp32 accumulators O_i (D columns):
-//   D = 128: S (128, shared by Q0 and Q1) | P0 P1 (2x64) | O0 O1 (2x128) = 512
-//   D =  64: S0 S1 (2x128)                | P0 P1 (2x64) | O0 O1 (2x64)  = 512
+// S = Q_i K_j^T (128 fp32 columns, one buffer shared by Q0 and Q1), one
+// buffer of P_i per query tile (64 columns of packed 16-bit pairs) and the
+// fp32 accumulators O_i (D columns):
+//   D = 128: S (128) | P0 P1 (2x64) | O0 O1 (2x128) = 512 columns
+//   D =  64: S (128) | P0 P1 (2x64) | O0 O1 (2x64)  = 384 columns
 // P never aliases S, so a QK product only waits until the previous scores in
-// its S buffer were copied to registers by their softmax warpgroup, never for
-// a PV product; PV_i(j) is issued once P_i(j) is written.  Both softmax
-// warpgroups then run their tiles back to back while the tensor core computes
-// the next scores and the previous PV products.
+// the S buffer were copied to registers by their softmax warpgroup, never for
+// a PV product; PV_i(j) is issued once P_i(j) is written.  The shared S buffer
+// makes the two softmax warpgroups alternate (S0(j), S1(j), S0(j+1), ...), so
+// the warps that share an SM sub-partition do not run their exponentials at
+// the same time, while the tensor core computes the next scores and the
+// previous PV products.
 // The running max is updated lazily: O and the row sum are rescaled only when
 // the max grows by more than 2^8, which keeps the unnormalised P in range and
 // makes rescaling rare; the final O / l is exact either way.
