@@ -56,7 +56,10 @@ enum {
 
 /* Bits the kernel ORs into *error_word (when error_word != NULL). */
 enum {
-  B200_ATTN_DEVERR_WAIT_TIMEOUT = 1
+  B200_ATTN_DEVERR_WAIT_TIMEOUT = 1,
+  /* checked build only: a TMA coordinate, shared-memory tile address or
+   * tensor-memory column range failed its check; the access was skipped */
+  B200_ATTN_DEVERR_BOUNDS = 2
 };
 
 typedef struct b200_attn_fwd_params {

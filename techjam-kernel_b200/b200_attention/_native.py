@@ -25,6 +25,7 @@ ERR_LAUNCH = 5
 ERR_TIMEOUT = 6
 
 DEVERR_WAIT_TIMEOUT = 1
+DEVERR_BOUNDS = 2
 
 # Every symbol the header declares; the CPU test checks the library exports them.
 EXPORTED_SYMBOLS = (
@@ -69,6 +70,28 @@ _lib = None
 _lock = threading.Lock()
 
 
+def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
+    """Declare the argument and result types of every exported entry point."""
+    lib.b200_attn_abi_version.restype = ctypes.c_int32
+    lib.b200_attn_abi_version.argtypes = []
+    lib.b200_attn_query.restype = ctypes.c_int32
+    lib.b200_attn_query.argtypes = [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32]
+    lib.b200_attn_check.restype = ctypes.c_int32
+    lib.b200_attn_check.argtypes = [ctypes.POINTER(FwdParams)]
+    lib.b200_attn_fwd.restype = ctypes.c_int32
+    lib.b200_attn_fwd.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_void_p]
+    lib.b200_attn_error_string.restype = ctypes.c_char_p
+    lib.b200_attn_error_string.argtypes = [ctypes.c_int32]
+    lib.b200_attn_launches_per_call.restype = ctypes.c_int32
+    lib.b200_attn_launches_per_call.argtypes = [ctypes.POINTER(FwdParams)]
+    lib.b200_attn_last_error_detail.restype = ctypes.c_char_p
+    lib.b200_attn_last_error_detail.argtypes = []
+    lib.b200_attn_selftest_stall.restype = ctypes.c_int32
+    lib.b200_attn_selftest_stall.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_int32,
+                                             ctypes.c_void_p]
+    return lib
+
+
 def load_library() -> ctypes.CDLL:
     """Load the native library (once).  Raises if it has not been built."""
     global _lib
@@ -82,26 +105,16 @@ def load_library() -> ctypes.CDLL:
                 f"{LIB_PATH.name} is not built; run `python -m b200_attention.build` "
                 "or __graft_entry__.build()"
             )
-        lib = ctypes.CDLL(str(LIB_PATH))
-        lib.b200_attn_abi_version.restype = ctypes.c_int32
-        lib.b200_attn_abi_version.argtypes = []
-        lib.b200_attn_query.restype = ctypes.c_int32
-        lib.b200_attn_query.argtypes = [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32]
-        lib.b200_attn_check.restype = ctypes.c_int32
-        lib.b200_attn_check.argtypes = [ctypes.POINTER(FwdParams)]
-        lib.b200_attn_fwd.restype = ctypes.c_int32
-        lib.b200_attn_fwd.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_void_p]
-        lib.b200_attn_error_string.restype = ctypes.c_char_p
-        lib.b200_attn_error_string.argtypes = [ctypes.c_int32]
-        lib.b200_attn_launches_per_call.restype = ctypes.c_int32
-        lib.b200_attn_launches_per_call.argtypes = [ctypes.POINTER(FwdParams)]
-        lib.b200_attn_last_error_detail.restype = ctypes.c_char_p
-        lib.b200_attn_last_error_detail.argtypes = []
-        lib.b200_attn_selftest_stall.restype = ctypes.c_int32
-        lib.b200_attn_selftest_stall.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_int32,
-                                                 ctypes.c_void_p]
-        _lib = lib
-        return lib
+        _lib = _bind(ctypes.CDLL(str(LIB_PATH)))
+        return _lib
+
+
+def load_checked_library() -> ctypes.CDLL:
+    """The bounds-checked build of the same library (tests only)."""
+    path = LIB_PATH.with_name("libb200_attention_checked.so")
+    if not path.exists():
+        raise RuntimeError(f"{path.name} is not built; run `python -m b200_attention.build`")
+    return _bind(ctypes.CDLL(str(path)))
 
 
 def error_text(code: int) -> str:

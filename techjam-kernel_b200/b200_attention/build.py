@@ -19,6 +19,10 @@ CSRC = PRODUCT_DIR / "csrc"
 INCLUDE = REPO_ROOT / "include"
 LIB_NAME = "libb200_attention.so"
 LIB_PATH = PACKAGE_DIR / LIB_NAME
+# Same source with every TMA coordinate, shared-memory tile address and
+# tensor-memory column range checked on the device (for tests; a failed check
+# sets B200_ATTN_DEVERR_BOUNDS in the error word instead of faulting).
+CHECKED_LIB_PATH = PACKAGE_DIR / "libb200_attention_checked.so"
 
 SOURCES = ("attn_fwd_sm100.cu",)
 HEADERS = ("sm100_ptx.cuh",)
@@ -51,19 +55,22 @@ def _inputs() -> list[Path]:
     return files
 
 
-def is_stale() -> bool:
-    if not LIB_PATH.exists():
+def is_stale(path: Path = LIB_PATH) -> bool:
+    if not path.exists():
         return True
-    built = LIB_PATH.stat().st_mtime
+    built = path.stat().st_mtime
     return any(f.stat().st_mtime > built for f in _inputs())
 
 
-def build_native(force: bool = False, verbose: bool = False) -> Path:
-    """Compile ``libb200_attention.so`` next to this file (skipped when fresh)."""
-    if not force and not is_stale():
-        return LIB_PATH
-    tmp = LIB_PATH.with_suffix(".so.tmp")
-    cmd = [_nvcc(), *NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}",
+def build_native(force: bool = False, verbose: bool = False, checked: bool = False) -> Path:
+    """Compile ``libb200_attention.so`` (or, with ``checked``, the bounds-checked
+    ``libb200_attention_checked.so``) next to this file; skipped when fresh."""
+    out = CHECKED_LIB_PATH if checked else LIB_PATH
+    if not force and not is_stale(out):
+        return out
+    tmp = out.with_suffix(".so.tmp")
+    defines = ["-DB200_ATTN_CHECKED=1"] if checked else []
+    cmd = [_nvcc(), *NVCC_FLAGS, *defines, f"-I{INCLUDE}", f"-I{CSRC}",
            *[str(CSRC / s) for s in SOURCES], "-o", str(tmp)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
@@ -73,12 +80,12 @@ def build_native(force: bool = False, verbose: bool = False) -> Path:
         raise RuntimeError(f"nvcc failed ({proc.returncode}):\n{proc.stderr[-8000:]}")
     if verbose and proc.stderr:
         print(proc.stderr)
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, out)
+    return out
 
 
 if __name__ == "__main__":
     import sys
 
-    build_native(force="--force" in sys.argv, verbose="-v" in sys.argv)
-    print(LIB_PATH)
+    print(build_native(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_native(force="--force" in sys.argv, checked=True))

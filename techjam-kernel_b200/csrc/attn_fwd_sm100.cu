@@ -82,6 +82,15 @@ constexpr int kPolyPer8 = B200_ATTN_POLY_PER8;
 // (Softmax warps keep suspending waits: their polling would take issue slots
 // from the other softmax warpgroup on the same SM sub-partition.)
 constexpr int kIssuerSpin = B200_ATTN_ISSUER_SPIN ? 4096 : 0;
+#ifndef B200_ATTN_CHECKED
+#define B200_ATTN_CHECKED 0
+#endif
+// Checked build (libb200_attention_checked.so): every TMA coordinate, shared-
+// memory tile address and tensor-memory column range is verified before use.
+// A failed check ORs B200_ATTN_DEVERR_BOUNDS into the error word, sets the CTA
+// abort flag and skips the access; the kernel then winds down through its
+// bounded waits.  No trap, no device assert.
+constexpr bool kChecked = B200_ATTN_CHECKED != 0;
 #ifndef B200_ATTN_GROUP_MB
 #define B200_ATTN_GROUP_MB 48
 #endif
@@ -394,6 +403,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile uint32_t* abort_flag = misc + 1;
   const uint32_t bar0 = sbase + C::kOffBar;
   auto bar = [&](int idx) { return bar0 + 8u * static_cast<uint32_t>(idx); };
+  // checked builds: true when the access may proceed
+  auto chk = [&](bool cond) {
+    if constexpr (kChecked) {
+      if (!cond) {
+        if (args.err) atomicOr(args.err, B200_ATTN_DEVERR_BOUNDS);
+        *abort_flag = 1u;
+      }
+      return cond;
+    } else {
+      return true;
+    }
+  };
+  // a whole tile of `bytes` at smem address `a`, 1024-byte aligned (128-byte
+  // swizzle atoms), inside [lo, hi)
+  auto tile_ok = [&](uint32_t a, uint32_t bytes, uint32_t lo, uint32_t hi) {
+    return a >= lo && a + bytes <= hi && ((a - sbase) & 1023u) == 0u;
+  };
+  auto coord_ok = [&](int x, int row, int hh, int bb, int row_hi) {
+    return x >= 0 && x + 64 <= D && (x & 63) == 0 && row >= 0 && row < row_hi && hh >= 0 &&
+           hh < args.heads && bb >= 0 && bb < args.batch;
+  };
 
   const uint8_t* mrow = nullptr;
   if constexpr (kMask) mrow = args.mask + static_cast<int64_t>(b) * args.mask_sb;
@@ -476,9 +506,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int c = 0; c < C::kChunks; ++c)
-          ptx::tma_load_4d(sbase + C::kOffQ + i * C::kQTileBytes + c * C::kQChunkBytes, &tm_q,
-                           bar(C::kBarQ), 64 * c, q0 + kBlockM * i, h, b);
+        for (int c = 0; c < C::kChunks; ++c) {
+          const uint32_t dst = sbase + C::kOffQ + i * C::kQTileBytes + c * C::kQChunkBytes;
+          if (chk(tile_ok(dst, C::kQChunkBytes, sbase + C::kOffQ, sbase + C::kOffRing) &&
+                  coord_ok(64 * c, q0 + kBlockM * i, h, b, args.num_q_blocks * kRowsPerCta)))
+            ptx::tma_load_4d(dst, &tm_q, bar(C::kBarQ), 64 * c, q0 + kBlockM * i, h, b);
+        }
       uint32_t L = 0;
       bool ok = true;
       for (int j = 0; ok && j < n_max; ++j) {
@@ -495,9 +528,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const CUtensorMap* tm = kv ? &tm_v : &tm_k;
 #pragma unroll
-          for (int c = 0; c < C::kChunks; ++c)
-            ptx::tma_load_4d(sbase + C::kOffRing + s * C::kKVTileBytes + c * C::kKVChunkBytes, tm,
-                             bar(C::kBarSlotFull + s), 64 * c, BN * j, h, b);
+          for (int c = 0; c < C::kChunks; ++c) {
+            const uint32_t dst = sbase + C::kOffRing + s * C::kKVTileBytes + c * C::kKVChunkBytes;
+            if (chk(tile_ok(dst, C::kKVChunkBytes, sbase + C::kOffRing, sbase + C::kOffBar) &&
+                    coord_ok(64 * c, BN * j, h, b, S)))
+              ptx::tma_load_4d(dst, tm, bar(C::kBarSlotFull + s), 64 * c, BN * j, h, b);
+          }
           ++L;
         }
       }
@@ -540,6 +576,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tc_fence_after();
           const uint32_t qaddr = sbase + C::kOffQ + i * C::kQTileBytes;
           const uint32_t kaddr = sbase + C::kOffRing + ks * C::kKVTileBytes;
+          if (!chk(tile_ok(qaddr, C::kQTileBytes, sbase + C::kOffQ, sbase + C::kOffRing) &&
+                   tile_ok(kaddr, C::kKVTileBytes, sbase + C::kOffRing, sbase + C::kOffBar) &&
+                   C::col_s(i) + BN <= kTmemCols)) {
+            ok = false;
+            break;
+          }
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t qo = (kk >> 2) * C::kQChunkBytes + (kk & 3) * 32;
@@ -580,6 +622,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           ptx::tc_fence_after();
+          if (!chk(tile_ok(vaddr, C::kKVTileBytes, sbase + C::kOffRing, sbase + C::kOffBar) &&
+                   C::col_p(i, j % PB) + BN / 2 <= kTmemCols && C::col_o(i) + D <= kTmemCols)) {
+            ok = false;
+            break;
+          }
           const uint32_t pcol = tmem + C::col_p(i, j % PB);
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
@@ -879,8 +926,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::named_barrier_sync(1 + i, kBlockM);
       if (rl == 0 && qstart < S) {
 #pragma unroll
-        for (int cb = 0; cb < C::kChunks; ++cb)
-          ptx::tma_store_4d(&tm_o, stage + cb * C::kQChunkBytes, 64 * cb, qstart, h, b);
+        for (int cb = 0; cb < C::kChunks; ++cb) {
+          const uint32_t src = stage + cb * C::kQChunkBytes;
+          if (chk(tile_ok(src, C::kQChunkBytes, sbase + C::kOffQ, sbase + C::kOffRing) &&
+                  coord_ok(64 * cb, qstart, h, b, S)))
+            ptx::tma_store_4d(&tm_o, src, 64 * cb, qstart, h, b);
+        }
         ptx::bulk_commit_group();
         ptx::bulk_wait_group_read_all();  // shared memory may go once the store has read it
       }

@@ -1,0 +1,56 @@
+"""Bounds-checked build on odd shapes (the stand-in for a sanitizer, which is
+closed on this pool).
+
+``libb200_attention_checked.so`` is the same kernel source compiled with every
+TMA coordinate, shared-memory tile address and tensor-memory column range
+verified on the device; a failed check sets ``B200_ATTN_DEVERR_BOUNDS`` in the
+error word and skips the access.  Each case must leave the word clear and match
+the oracle.
+"""
+
+import ctypes
+
+import pytest
+import torch
+
+from b200_attention import _native
+from b200_attention.fused_attention import device_error_word, make_params, read_device_errors
+from oracle.reference_attention import reference_attention, zero_masked_rows
+from parity import assert_close, prefix_mask, seeded_qkv
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    # (B, H, S, D, causal, lengths, zero_masked_queries)
+    (1, 1, 1, 128, True, None, False),
+    (2, 2, 33, 64, False, None, False),
+    (1, 3, 97, 128, True, None, False),
+    (2, 1, 129, 64, True, None, False),
+    (1, 2, 255, 128, False, None, False),
+    (2, 2, 257, 128, True, [257, 100], False),
+    (3, 2, 700, 64, False, [700, 333, 1], True),
+    (1, 2, 1000, 128, True, None, False),
+    (2, 1, 1536, 128, False, [1536, 700], True),
+]
+
+
+@pytest.mark.parametrize("B,H,S,D,causal,lengths,zero_q", CASES)
+def test_checked_build_odd_shapes(B, H, S, D, causal, lengths, zero_q):
+    dev = torch.device("cuda", 0)
+    lib = _native.load_checked_library()
+    q, k, v = seeded_qkv((B, H, S, D), torch.bfloat16, 41 + S)
+    mask = prefix_mask(B, S, lengths) if lengths else None
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    md = mask.to(dev) if mask is not None else None
+    out = torch.full((B, H, S, D), float("nan"), device=dev, dtype=torch.bfloat16)
+    read_device_errors(dev)
+    params = make_params(qd, kd, vd, out, md, causal, D ** -0.5, zero_q, device_error_word(dev))
+    rc = lib.b200_attn_fwd(ctypes.byref(params),
+                           ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+    assert rc == _native.OK
+    torch.cuda.synchronize(dev)
+    assert read_device_errors(dev) == 0, "a bounds check failed"
+    ref = reference_attention(q, k, v, mask, causal, D ** -0.5)
+    if zero_q:
+        ref = zero_masked_rows(ref, mask)
+    assert_close(out, ref, f"checked B{B} H{H} S{S} D{D}")
