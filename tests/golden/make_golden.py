@@ -1,6 +1,6 @@
 """Generate the golden fixtures from the reference itself (run in the build container).
 
-    python tests/golden/make_golden.py [--reference /path/to/reference]
+    python tests/golden/make_golden.py --reference /path/to/reference
 
 Writes, next to this script:
 
@@ -79,7 +79,7 @@ def to_bits(t: torch.Tensor) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="checkout of the reference repository")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from model.attention_dispatch import AttentionModelSpec, AttentionRuntime, select_attention_stack_plan

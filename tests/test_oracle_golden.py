@@ -69,7 +69,7 @@ def test_zero_masked_rows():
     assert z[0, 0, 2:].abs().sum() == 0 and z[1, 0, 1].abs().sum() == 0 and z[1, 0, 2].sum() == 2
 
 
-def test_flop_counts_match_survey_totals():
+def test_flop_counts_match_the_configuration_totals():
     # cfg2 137.4 GFLOP causal, north-star 2199.0 GFLOP, cfg4 8796 GFLOP
     assert abs(attention_flops(8, 16, 2048, 128, True) / 1e9 - 137.4) < 0.1
     assert abs(attention_flops(8, 16, 8192, 128, True) / 1e9 - 2199.0) < 0.1
