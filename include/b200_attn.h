@@ -101,8 +101,10 @@ B200_ATTN_API int32_t b200_attn_query(int32_t dtype, int64_t head_dim, int32_t c
  * (model/triton_fused_attention.py:1217-1253) for the device path. */
 B200_ATTN_API int32_t b200_attn_check(const b200_attn_fwd_params* p);
 
-/* Launch the forward on `stream` (a cudaStream_t; NULL = legacy default stream).
- * Asynchronous: no device synchronisation, no allocation.  Replaces the kernel
+/* Launch the forward on `stream` (a cudaStream_t of the tensors' device; NULL =
+ * legacy default stream).  The device is taken from the q pointer; the caller's
+ * current device is left as it was.  Asynchronous: no device synchronisation,
+ * no allocation.  Replaces the kernel
  * launch of triton_fused_attention (model/triton_fused_attention.py:1968-2001). */
 B200_ATTN_API int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream);
 

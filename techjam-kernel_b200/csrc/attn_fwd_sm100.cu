@@ -1128,9 +1128,19 @@ extern "C" int32_t b200_attn_launches_per_call(const b200_attn_fwd_params* p) {
 namespace b200attn {
 namespace {
 
-// Validates p, selects its device and fills the tensor maps and kernel
-// arguments; returns a B200_ATTN_* code.
-int32_t prepare(const b200_attn_fwd_params* p, CUtensorMap maps[4], KernelArgs& a, int& dev_out) {
+// Restores the caller's current device when a call had to switch to the
+// tensors' device.
+struct DeviceGuard {
+  int prev = -1;
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+// Validates p, selects its device (restored by `guard` when the call ends) and
+// fills the tensor maps and kernel arguments; returns a B200_ATTN_* code.
+int32_t prepare(const b200_attn_fwd_params* p, CUtensorMap maps[4], KernelArgs& a, int& dev_out,
+                DeviceGuard& guard) {
   int32_t rc = b200_attn_check(p);
   if (rc != B200_ATTN_OK) return rc;
 
@@ -1150,6 +1160,7 @@ int32_t prepare(const b200_attn_fwd_params* p, CUtensorMap maps[4], KernelArgs& 
       set_error("cudaSetDevice failed");
       return B200_ATTN_ERR_DEVICE;
     }
+    guard.prev = cur;
   }
   std::call_once(g_dev[dev].probed, [dev] {
     int major = 0;
@@ -1207,7 +1218,8 @@ extern "C" int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream) {
   CUtensorMap maps[4];
   KernelArgs a;
   int dev = 0;
-  const int32_t rc = prepare(p, maps, a, dev);
+  DeviceGuard guard;
+  const int32_t rc = prepare(p, maps, a, dev, guard);
   if (rc != B200_ATTN_OK) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (p->head_dim == 128) return dispatch_flags<Cfg128>(maps, a, p, dev, s);
@@ -1222,7 +1234,8 @@ extern "C" int32_t b200_attn_selftest_stall(const b200_attn_fwd_params* p, int32
   CUtensorMap maps[4];
   KernelArgs a;
   int dev = 0;
-  const int32_t rc = prepare(p, maps, a, dev);
+  DeviceGuard guard;
+  const int32_t rc = prepare(p, maps, a, dev, guard);
   if (rc != B200_ATTN_OK) return rc;
   a.skip_load = skipped_load;
   return launch_one<Cfg128, true, false, true, true>(maps, a, dev,
