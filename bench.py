@@ -409,6 +409,10 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
         cpu = CpuReference(cfg, args.seed).measure(args.cpu_budget, min_reps=3)
     peaks, peak_src = load_peaks()
     peak = peaks["bf16_tflops"]
+    traffic = None
+    prof = ROOT / "profiles" / "attn_fwd_sm100_cfg5_traffic.json"
+    if prof.exists() and world == 1:  # captured at the N = 1 per-layer shape
+        traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -429,7 +433,7 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
         "attention": {"tflops": attn_tflops, "ms_per_layer": attn_ms,
                       "share_of_forward": cfg["layers"] * attn_ms / ms_per_step},
         "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": peak, "unit": "TFLOP/s",
-                     "frac": attn_tflops / peak, "traffic": None,
+                     "frac": attn_tflops / peak, "traffic": traffic,
                      "kernel": "attn_fwd_sm100_kernel at the per-rank attention shape",
                      "peak_source": f"{peak_src} bf16_tflops (burst, kernel timed alone)"},
         "cpu_baseline": cpu,
@@ -643,7 +647,11 @@ def main(argv=None) -> int:
     traffic = None
     prof = ROOT / "profiles" / f"attn_fwd_sm100_{args.workload}_traffic.json"
     if prof.exists():
+        # captured for the whole N = 1 launch; a head-sharded rank processes
+        # H / cfg["H"] of the heads, and the traffic scales with them
         traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
+        if traffic is not None:
+            traffic = traffic * H / cfg["H"]
     lib = _native.load_library()
     launches = args.steps  # one kernel launch per step (b200_attn_launches_per_call == 1)
 
