@@ -89,8 +89,10 @@ typedef struct b200_attn_fwd_params {
 /* ABI version (B200_ATTN_ABI_VERSION). */
 B200_ATTN_API int32_t b200_attn_abi_version(void);
 
-/* Host-only envelope query used by the planner: 1 when the kernel supports
- * (dtype, head_dim) for the given causal/mask flags, else 0.  Makes no CUDA call.
+/* Host-only envelope query: 1 when the kernel computes (dtype, head_dim)
+ * natively for the given causal/mask flags (head_dim 64 or 128), else 0.  Makes
+ * no CUDA call.  (The Python operator and planner also accept other multiples
+ * of 8 up to 128 by zero-padding them to 64 or 128.)
  * Replaces the support test of triton_fused_attention
  * (model/triton_fused_attention.py:1906-1921) and the planner's envelope
  * (model/attention_dispatch.py:399-459). */

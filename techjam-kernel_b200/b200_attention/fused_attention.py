@@ -27,7 +27,11 @@ import torch
 from . import _native
 
 SUPPORTED_DTYPES = {torch.bfloat16: _native.DTYPE_BF16, torch.float16: _native.DTYPE_FP16}
-SUPPORTED_HEAD_DIMS = (64, 128)
+NATIVE_HEAD_DIMS = (64, 128)  # what the kernel computes directly
+# Other head dims (multiples of 8 up to 128) are zero-padded to the next native
+# size: zero columns add nothing to Q K^T, and V's zero columns give output
+# columns that are dropped; the softmax scale stays that of the true head dim.
+SUPPORTED_HEAD_DIMS = tuple(range(8, 129, 8))
 BLOCK_M = 128  # query rows per tile (two tiles per CTA)
 BLOCK_N = 128  # keys per K/V tile
 
@@ -79,7 +83,8 @@ def unsupported_reason(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Opt
     if q.dtype not in SUPPORTED_DTYPES:
         return f"dtype {q.dtype} is outside the kernel envelope (bfloat16, float16)"
     if q.shape[-1] not in SUPPORTED_HEAD_DIMS:
-        return f"head_dim {q.shape[-1]} is outside the kernel envelope {SUPPORTED_HEAD_DIMS}"
+        return (f"head_dim {q.shape[-1]} is outside the kernel envelope "
+                "(multiples of 8 up to 128)")
     if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
         return "q/k/v must have a contiguous last dimension"
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
@@ -99,6 +104,24 @@ def _capability_major(device: torch.device) -> int:
     if major is None:
         major = _capability[index] = torch.cuda.get_device_capability(index)[0]
     return major
+
+
+def _padded_head_dim(q, k, v, valid_token_mask, causal, scale, output_bshd,
+                     zero_masked_queries, out):
+    """Head dims other than 64/128: run the kernel on copies zero-padded to the
+    next native head dim and keep the first ``head_dim`` output columns."""
+    head_dim = q.shape[-1]
+    padded = 64 if head_dim <= 64 else 128
+    pad = lambda t: torch.nn.functional.pad(t, (0, padded - head_dim))
+    res = b200_fused_attention(pad(q), pad(k), pad(v), valid_token_mask, causal, scale,
+                               output_bshd, zero_masked_queries=zero_masked_queries)
+    res = res[..., :head_dim]
+    if out is not None:
+        if tuple(out.shape) != tuple(res.shape):
+            raise ValueError(f"out must have shape {tuple(res.shape)}")
+        out.copy_(res)
+        return out
+    return res.contiguous()
 
 
 def device_error_word(device: torch.device) -> torch.Tensor:
@@ -205,6 +228,9 @@ def b200_fused_attention(
         raise ValueError(f"unsupported sm_100a attention invocation: {reason}")
     if zero_masked_queries and valid_token_mask is None:
         raise ValueError("zero_masked_queries requires valid_token_mask")
+    if head_dim not in NATIVE_HEAD_DIMS:
+        return _padded_head_dim(q, k, v, valid_token_mask, causal, scale, output_bshd,
+                                zero_masked_queries, out)
 
     if output_bshd:
         shape = (batch, seq_len, heads, head_dim)

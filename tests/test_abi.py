@@ -67,10 +67,15 @@ def test_abi_version(lib):
 
 
 def test_query_agrees_with_planner_envelope(lib):
+    """The C ABI reports the kernel's native head dims; the planner's envelope
+    adds the head dims the operator zero-pads to them (multiples of 8 up to 128)."""
     for dtype in (_native.DTYPE_BF16, _native.DTYPE_FP16, 7):
         for d in (16, 32, 64, 96, 128, 256):
-            want = 1 if dtype in (0, 1) and d in SM100_HEAD_DIMS else 0
-            assert lib.b200_attn_query(dtype, d, 1, 0) == want
+            native = 1 if dtype in (0, 1) and d in (64, 128) else 0
+            assert lib.b200_attn_query(dtype, d, 1, 0) == native
+            if native:
+                assert d in SM100_HEAD_DIMS
+    assert set(SM100_HEAD_DIMS) == set(range(8, 129, 8))
 
 
 def _params(**kw):

@@ -93,3 +93,24 @@ def test_fully_masked_rows_are_nan():
     out, ref = _run((2, 1, 130, 128), torch.bfloat16, False, lengths=[130, 0], seed=2)
     assert torch.isnan(out[1].float()).all() and torch.isnan(ref[1].float()).all()
     assert_close(out, ref, "nan rows")
+
+
+@pytest.mark.parametrize("D", [8, 16, 32, 96])
+@pytest.mark.parametrize("causal", [False, True])
+def test_padded_head_dims(D, causal):
+    """Head dims the kernel does not compute natively are zero-padded to 64 or
+    128; the result must equal attention at the true head dim."""
+    out, ref = _run((2, 3, 300, D), torch.bfloat16, causal, lengths=[300, 123])
+    assert out.shape == ref.shape
+    assert_close(out, ref, f"D={D}")
+
+
+def test_padded_head_dim_bshd_and_out():
+    q, k, v = seeded_qkv((2, 4, 128, 32), torch.bfloat16, 77)
+    ref = reference_attention(q, k, v, None, True, 32 ** -0.5)
+    out = torch.empty((2, 128, 4, 32), device=DEV, dtype=torch.bfloat16)
+    res = b200_fused_attention(q.to(DEV), k.to(DEV), v.to(DEV), None, True, output_bshd=True,
+                               out=out)
+    torch.cuda.synchronize()
+    assert res is out and out.is_contiguous()
+    assert_close(out.transpose(1, 2), ref, "D=32 BSHD")
