@@ -51,7 +51,21 @@ WORKLOADS = {
     # global batch 8 split over the ranks (data parallel)
     "cfg5": dict(B=8, H=16, S=2048, D=64, causal=True, masked=False, shard="batch_split",
                  layers=12, d_model=1024, ffn=4096, vocab=32000),
+    # the reference's only published attention timing (fp16 two-pass tiled
+    # attention, docs/TECH_REPORT.md:98-111): 0.590592 ms on an RTX 5070 Ti
+    "tr": dict(B=64, H=4, S=1024, D=32, causal=True, masked=False, shard="batch", dtype="float16",
+               published_ms=0.590592, published_hw="RTX 5070 Ti (sm_120), fp16 two-pass Triton"),
 }
+
+
+def cfg_dtype(cfg: dict):
+    import torch
+
+    return getattr(torch, cfg.get("dtype", "bfloat16"))
+
+
+def dtype_tag(cfg: dict) -> str:
+    return {"bfloat16": "bf16", "float16": "fp16"}[cfg.get("dtype", "bfloat16")]
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -178,7 +192,7 @@ class CpuReference:
         self.S, self.D, self.causal = S, D, causal
         heads = max(1, min(cfg["H"], int(2 ** 31 // (S * S * 12))))
         gen = torch.Generator("cpu").manual_seed(seed)
-        self.q, self.k, self.v = (torch.randn((1, heads, S, D), generator=gen).to(torch.bfloat16)
+        self.q, self.k, self.v = (torch.randn((1, heads, S, D), generator=gen).to(cfg_dtype(cfg))
                                   for _ in range(3))
         lengths = valid_lengths(cfg, seed)
         self.mask = None
@@ -193,7 +207,7 @@ class CpuReference:
             self.flop = 4.0 * heads * D * L * L
         else:
             self.flop = flops_for(cfg, 1, heads, None)
-        self.desc = (f"oracle.reference_attention (torch CPU, bf16, reference op order) on "
+        self.desc = (f"oracle.reference_attention (torch CPU, {dtype_tag(cfg)}, reference op order) on "
                      f"[1,{heads},{S},{D}] causal={causal}"
                      + (f" rows {self.rows[0]}..{self.rows[1] - 1}" if self.rows else "")
                      + (f" key-mask L={lengths[0]}" if self.mask is not None else "")
@@ -234,7 +248,7 @@ def run_reference_arm(args, cfg: dict, rank: int, world: int) -> int:
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak" if cfg["shard"] != "heads" else "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded torch.randn N(0,1))",
+        "vs_baseline": None, "dtype": dtype_tag(cfg), "data": "synthetic (seeded torch.randn N(0,1))",
         "config": {"workload": args.workload, **{k: cfg[k] for k in ("B", "H", "S", "D", "causal")},
                    "impl_path": "oracle.reference_attention on host CPU cores"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": ref.torch.get_num_threads(),
@@ -286,7 +300,7 @@ def run_dense_arm(args, cfg: dict, rank: int, world: int) -> int:
     lengths = valid_lengths(cfg, args.seed)
     flop = flops_for(cfg, B, H, lengths)
     gen = torch.Generator(device=dev).manual_seed(args.seed)
-    q, k, v = (torch.randn((B, H, S, D), generator=gen, device=dev).to(torch.bfloat16)
+    q, k, v = (torch.randn((B, H, S, D), generator=gen, device=dev).to(cfg_dtype(cfg))
                for _ in range(3))
     mask = None
     if lengths is not None:
@@ -308,7 +322,7 @@ def run_dense_arm(args, cfg: dict, rank: int, world: int) -> int:
     line = {
         "impl": "torch-dense", "metric": METRIC, "value": flop / (ms * 1e-3) / 1e12, "unit": UNIT,
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded torch.randn N(0,1))",
+        "higher_is_better": True, "dtype": dtype_tag(cfg), "data": "synthetic (seeded torch.randn N(0,1))",
         "config": {"workload": args.workload, **{k: cfg[k] for k in ("B", "H", "S", "D", "causal")},
                    "per_gpu_batch_heads": [B, H],
                    "impl_path": "dense torch CUDA ops in _reference_attention's order (cuBLAS GEMMs)"},
@@ -520,13 +534,13 @@ def main(argv=None) -> int:
     sets = []
     for _ in range(n_sets):
         q, k, v = (torch.randn((B, H, S, D), generator=gen, device=dev, dtype=torch.float32)
-                   .to(torch.bfloat16) for _ in range(3))
+                   .to(cfg_dtype(cfg)) for _ in range(3))
         sets.append((q, k, v))
     mask = None
     if lengths is not None:
         mask = (torch.arange(S, device=dev)[None, :] <
                 torch.tensor(lengths, device=dev)[:, None])
-    outs = [torch.empty((B, S, H, D), device=dev, dtype=torch.bfloat16) for _ in range(n_sets)]
+    outs = [torch.empty((B, S, H, D), device=dev, dtype=cfg_dtype(cfg)) for _ in range(n_sets)]
     zero_q = mask is not None
 
     def step(i):
@@ -611,7 +625,7 @@ def main(argv=None) -> int:
     e2e_steps = args.e2e_steps or max(3, min(args.steps, 20))
     hq, hk, hv = (t.cpu().pin_memory() for t in sets[0])
     hmask = mask.cpu().pin_memory() if mask is not None else None
-    hout = torch.empty((B, S, H, D), dtype=torch.bfloat16).pin_memory()
+    hout = torch.empty((B, S, H, D), dtype=cfg_dtype(cfg)).pin_memory()
     h2d = 3 * hq.numel() * hq.element_size() + (hmask.numel() if hmask is not None else 0)
     d2h = hout.numel() * hout.element_size()
 
@@ -655,6 +669,10 @@ def main(argv=None) -> int:
     lib = _native.load_library()
     launches = args.steps  # one kernel launch per step (b200_attn_launches_per_call == 1)
 
+    vs_baseline = None
+    if "published_ms" in cfg:
+        # the reference's own number for this shape, on other hardware
+        vs_baseline = value / (flops_for(cfg, cfg["B"], cfg["H"], None) / (cfg["published_ms"] * 1e-3) / 1e12)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -670,8 +688,8 @@ def main(argv=None) -> int:
         "ms_per_step": ms_per_step,
         "higher_is_better": True,
         "scaling": scaling,
-        "vs_baseline": None,
-        "dtype": "bf16",
+        "vs_baseline": vs_baseline,
+        "dtype": dtype_tag(cfg),
         "data": "synthetic (seeded torch.randn N(0,1), no dataset)",
         "config": {
             "workload": args.workload, "B": cfg["B"], "H": cfg["H"], "S": S, "D": D,
@@ -682,6 +700,9 @@ def main(argv=None) -> int:
             "launch": "CUDA graph of the timed steps" if graph is not None else "eager, one operator call per step",
             "flop_per_step_job": flop_job,
             "valid_lengths": lengths,
+            **({"published_baseline": f"{cfg['published_hw']}: {cfg['published_ms']} ms per call "
+                                      "(vs_baseline compares across hardware)"}
+               if "published_ms" in cfg else {}),
         },
         "pct_of_bf16_peak": 100.0 * value / (peak * world),
         "roofline": {
