@@ -114,3 +114,41 @@ def test_padded_head_dim_bshd_and_out():
     torch.cuda.synchronize()
     assert res is out and out.is_contiguous()
     assert_close(out.transpose(1, 2), ref, "D=32 BSHD")
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_zero_masked_queries_causal(D):
+    out, ref = _run((3, 2, 600, D), torch.bfloat16, True, lengths=[600, 257, 1], seed=13, zero_q=True)
+    assert_close(out, ref, "zero_q causal")
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("D,dtype", [(64, torch.float16), (128, torch.bfloat16)])
+def test_arbitrary_key_masks(causal, D, dtype):
+    """Masks with holes (not a valid-length prefix), as the operator accepts any
+    boolean [B, S] key mask; rows that see no valid key are NaN like the reference."""
+    B, H, S = 2, 2, 389
+    q, k, v = seeded_qkv((B, H, S, D), dtype, 17)
+    gen = torch.Generator("cpu").manual_seed(99)
+    mask = torch.rand((B, S), generator=gen) < 0.6
+    mask[1, :5] = False  # early causal rows of batch 1 see no valid key -> NaN
+    ref = reference_attention(q, k, v, mask, causal, D ** -0.5)
+    out = b200_fused_attention(q.to(DEV), k.to(DEV), v.to(DEV), mask.to(DEV), causal)
+    torch.cuda.synchronize()
+    assert read_device_errors(DEV) == 0
+    assert_close(out, ref, "holes")
+
+
+def test_strided_mask_view():
+    """A mask that is a strided view (seq stride 2) goes through the scalar path."""
+    B, H, S, D = 2, 2, 300, 128
+    q, k, v = seeded_qkv((B, H, S, D), torch.bfloat16, 23)
+    wide = torch.zeros((B, 2 * S), dtype=torch.bool)
+    wide[0, 0:2 * 250:2] = True
+    wide[1, 0:2 * 77:2] = True
+    mask = wide[:, ::2]
+    assert mask.stride(1) == 2
+    ref = reference_attention(q, k, v, mask.contiguous(), False, D ** -0.5)
+    out = b200_fused_attention(q.to(DEV), k.to(DEV), v.to(DEV), wide.to(DEV)[:, ::2], False)
+    torch.cuda.synchronize()
+    assert_close(out, ref, "strided mask")
