@@ -152,3 +152,22 @@ def test_strided_mask_view():
     out = b200_fused_attention(q.to(DEV), k.to(DEV), v.to(DEV), wide.to(DEV)[:, ::2], False)
     torch.cuda.synchronize()
     assert_close(out, ref, "strided mask")
+
+
+def test_contract_errors_raise_not_crash():
+    """Contract violations come back as exceptions from the host-side checks;
+    nothing is launched."""
+    base = torch.zeros((1, 1, 64, 136), device=DEV, dtype=torch.bfloat16)
+    q = base[..., 1:129]  # 2-byte offset: not 16-byte aligned for TMA
+    ok = torch.zeros((1, 1, 64, 128), device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        b200_fused_attention(q, ok, ok, None, True)
+    with pytest.raises(ValueError):
+        b200_fused_attention(ok, ok, ok, None, True, scale=-1.0)
+    with pytest.raises(ValueError):
+        b200_fused_attention(ok.float(), ok.float(), ok.float(), None, True)
+    with pytest.raises(ValueError):
+        b200_fused_attention(ok, ok, ok, None, True, zero_masked_queries=True)
+    with pytest.raises(TypeError):
+        b200_fused_attention(ok, ok, ok, torch.ones((1, 64), device=DEV), True)
+    assert read_device_errors(DEV) == 0
