@@ -3,6 +3,9 @@
 - ``b200_fused_attention``: functional operator (reference: triton_fused_attention)
 - ``attention_dispatch``: planner (reference: model/attention_dispatch.py)
 - ``B200FusedSelfAttention``: module adapter (reference: TritonFusedSelfAttention)
+- ``b200_linear``: the block's linear layers with their elementwise epilogues
+  (bias, exact GELU, residual add, padded-row zeroing) fused into one kernel
 """
 
 from .fused_attention import b200_fused_attention, read_device_errors  # noqa: F401
+from .linear import b200_linear  # noqa: F401

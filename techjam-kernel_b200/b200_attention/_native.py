@@ -1,4 +1,4 @@
-"""ctypes binding of the C ABI in ``include/b200_attn.h``.
+"""ctypes binding of the C ABI in ``include/b200_attn.h`` and ``include/b200_linear.h``.
 
 This module is torch-free: it loads ``libb200_attention.so`` and describes the
 parameter struct.  The library is loaded from this directory only; a missing or
@@ -38,6 +38,17 @@ EXPORTED_SYMBOLS = (
     "b200_attn_last_error_detail",
     "b200_attn_selftest_stall",
 )
+# Every symbol ``include/b200_linear.h`` declares.
+LINEAR_SYMBOLS = (
+    "b200_linear_check",
+    "b200_linear_fwd",
+    "b200_linear_tile_n",
+)
+
+LINEAR_ACT_NONE = 0
+LINEAR_ACT_GELU = 1
+LINEAR_MASKED_ZERO = 0
+LINEAR_MASKED_KEEP_RESIDUAL = 1
 
 
 class FwdParams(ctypes.Structure):
@@ -66,6 +77,31 @@ class FwdParams(ctypes.Structure):
     ]
 
 
+class LinearParams(ctypes.Structure):
+    """Mirror of ``b200_linear_params``."""
+
+    _fields_ = [
+        ("x", ctypes.c_void_p),
+        ("w", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("residual", ctypes.c_void_p),
+        ("row_mask", ctypes.c_void_p),
+        ("y", ctypes.c_void_p),
+        ("m", ctypes.c_int64),
+        ("n", ctypes.c_int64),
+        ("k", ctypes.c_int64),
+        ("x_row_stride", ctypes.c_int64),
+        ("w_row_stride", ctypes.c_int64),
+        ("residual_row_stride", ctypes.c_int64),
+        ("y_row_stride", ctypes.c_int64),
+        ("dtype", ctypes.c_int32),
+        ("activation", ctypes.c_int32),
+        ("masked_rows", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("error_word", ctypes.c_void_p),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -89,6 +125,12 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.b200_attn_selftest_stall.restype = ctypes.c_int32
     lib.b200_attn_selftest_stall.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_int32,
                                              ctypes.c_void_p]
+    lib.b200_linear_check.restype = ctypes.c_int32
+    lib.b200_linear_check.argtypes = [ctypes.POINTER(LinearParams)]
+    lib.b200_linear_fwd.restype = ctypes.c_int32
+    lib.b200_linear_fwd.argtypes = [ctypes.POINTER(LinearParams), ctypes.c_void_p]
+    lib.b200_linear_tile_n.restype = ctypes.c_int32
+    lib.b200_linear_tile_n.argtypes = [ctypes.POINTER(LinearParams), ctypes.c_int32]
     return lib
 
 

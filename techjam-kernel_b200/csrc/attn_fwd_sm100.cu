@@ -964,13 +964,15 @@ using Cfg128 = Cfg<128, 128, 1, 5, true>;
 using Cfg64 = Cfg<64, 128, 1, 10, true>;
 
 // ------------------------------------------------------------------- host
-namespace {
-
+// Text of the calling thread's last host-side failure, shared by every entry
+// point of the library (b200_attn_last_error_detail).
 thread_local char g_last_error[256] = {0};
 
 void set_error(const char* msg) {
   std::snprintf(g_last_error, sizeof(g_last_error), "%s", msg);
 }
+
+namespace {
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
