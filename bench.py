@@ -352,7 +352,9 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
     S, D = cfg["S"], cfg["D"]
     dcfg = DecoderConfig(B, S, cfg["d_model"], H, cfg["ffn"], cfg["layers"], cfg["causal"],
                          vocab_size=cfg["vocab"])
-    model = init_normal_(Decoder(dcfg), seed=args.seed).to(device=dev, dtype=torch.bfloat16).eval()
+    fused = not args.unfused_epilogues
+    model = init_normal_(Decoder(dcfg, fused_epilogues=fused), seed=args.seed)
+    model = model.to(device=dev, dtype=torch.bfloat16).eval()
     flop_rank = dcfg.forward_flops()
     tot = torch.tensor([flop_rank], dtype=torch.float64, device=dev)
     if world > 1:
@@ -463,6 +465,9 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
                    "global_batch": cfg["B"], "per_rank_batch": B, "seq_len": S, "causal": True,
                    "parallelism": f"data-parallel batch split x{world}, no data-path collective",
                    "launch": "CUDA graph of the whole forward" if graph is not None else "eager",
+                   "epilogues": ("fused linear kernel: out_proj + residual, ffn_in + GELU "
+                                 "(QKV and ffn_out on cuBLAS)") if fused else
+                                "cuBLAS linear layers + separate GELU / add passes",
                    "l2": f"{n_sets} token sets; each forward streams ~0.4 GB of weights and activations (> L2)",
                    "flop_per_step_job": flop_job},
         "attention": {"tflops": attn_tflops, "ms_per_layer": attn_ms,
@@ -475,7 +480,8 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
         "e2e": {"value": flop_rank / (e2e_ms * 1e-3) / 1e12 * world, "unit": "TFLOP/s (decoder forward)",
                 "h2d_bytes_per_step": htok.numel() * htok.element_size(),
                 "d2h_bytes_per_step": hout.numel() * hout.element_size(), "ms_per_step": e2e_ms},
-        "gpu_launches": args.steps * cfg["layers"],
+        # per layer: the attention kernel, plus out_proj and ffn_in on the fused linear kernel
+        "gpu_launches": args.steps * cfg["layers"] * (3 if fused else 1),
         "clocks": sampler.summary(),
         "validation": {"finite": finite, "device_errors": errors},
     }
@@ -496,6 +502,9 @@ def main(argv=None) -> int:
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--graph", action="store_true",
                     help="replay the timed steps from a CUDA graph (launch-bound workloads)")
+    ap.add_argument("--unfused-epilogues", action="store_true",
+                    help="cfg5: run the block's linear layers on cuBLAS with separate GELU/add "
+                         "passes (the yardstick for the fused linear kernel)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

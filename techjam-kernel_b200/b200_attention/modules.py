@@ -14,7 +14,8 @@ Per layer the planner picks the executor:
   reference keeps per-projection views, :2287-2292); the sm_100a kernel writes
   the context directly in the [B, S, H, D] layout ``out_proj`` consumes;
   padded query rows are zeroed after ``out_proj`` exactly as the reference
-  does (:2456-2461).
+  does (:2456-2461).  ``residual_forward`` additionally folds the block's
+  residual add into the output projection (one fused linear kernel).
 * ``EXACT_REFERENCE`` / ``FP32_BASELINE_EXACT``: the planner routes inputs the
   kernel does not cover (autograd, fp32, other head sizes, non-CUDA devices) to
   the organiser's PyTorch operation order, as the reference planner does.
@@ -32,6 +33,7 @@ import torch.nn as nn
 from .attention_dispatch import (AttentionMode, AttentionModelSpec, AttentionRuntime, PlanScope,
                                  select_attention_stack_plan)
 from .fused_attention import b200_fused_attention
+from .linear import b200_linear, linear_supported
 
 _DTYPE_NAMES = {torch.float16: "float16", torch.bfloat16: "bfloat16", torch.float32: "float32"}
 
@@ -126,22 +128,50 @@ class B200FusedSelfAttention(nn.Module):
         batch, seq_len, _ = projected.shape
         return projected.view(batch, seq_len, self.num_heads, self.head_dim).transpose(1, 2)
 
-    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
-                causal: bool = False) -> torch.Tensor:
+    def _sm100_context(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor],
+                       causal: bool) -> torch.Tensor:
+        """Attention context [B, S, d] before ``out_proj`` on the sm_100a path."""
         batch, seq_len, _ = x.shape
+        weight, bias = self._stacked_qkv()
+        qkv = torch.nn.functional.linear(x, weight, bias).view(
+            batch, seq_len, 3, self.num_heads, self.head_dim)
+        q, k, v = (qkv[:, :, t].transpose(1, 2) for t in range(3))
+        context = b200_fused_attention(q, k, v, valid_token_mask, causal, self.scale,
+                                       output_bshd=True)
+        return context.view(batch, seq_len, self.d_model)
+
+    def _plan_mode(self, x: torch.Tensor, causal: bool) -> AttentionMode:
         needs_autograd = torch.is_grad_enabled() and (
             x.requires_grad or any(p.requires_grad for p in self.parameters()))
         _, plan = self._attention_plan(x, causal, needs_autograd)
+        return plan.mode
 
-        if plan.mode == AttentionMode.SM100_FUSED:
-            weight, bias = self._stacked_qkv()
-            qkv = torch.nn.functional.linear(x, weight, bias).view(
-                batch, seq_len, 3, self.num_heads, self.head_dim)
-            q, k, v = (qkv[:, :, t].transpose(1, 2) for t in range(3))
-            context = b200_fused_attention(q, k, v, valid_token_mask, causal, self.scale,
-                                           output_bshd=True)
-            context = context.view(batch, seq_len, self.d_model)
-        elif plan.mode in (AttentionMode.EXACT_REFERENCE, AttentionMode.FP32_BASELINE_EXACT):
+    def residual_forward(self, x: torch.Tensor, residual: torch.Tensor,
+                         valid_token_mask: Optional[torch.Tensor] = None,
+                         causal: bool = False) -> Optional[torch.Tensor]:
+        """``residual + self(x, valid_token_mask, causal)``, the first half of
+        the reference block (torch_transformer_benchmark.py:141), with the
+        output projection, its bias, the padded-row zeroing and the residual add
+        in one fused linear kernel (rows whose mask is False keep ``residual``
+        unchanged, as ``residual + 0`` does).  Returns None when this call does
+        not take the sm_100a path; the caller then runs the unfused sequence."""
+        if self._plan_mode(x, causal) != AttentionMode.SM100_FUSED:
+            return None
+        if not linear_supported(x, self.out_proj.weight) or residual.shape != x.shape \
+                or residual.dtype != x.dtype:
+            return None
+        context = self._sm100_context(x, valid_token_mask, causal)
+        return b200_linear(context, self.out_proj.weight, self.out_proj.bias, residual=residual,
+                           row_mask=valid_token_mask, masked_rows="residual")
+
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
+                causal: bool = False) -> torch.Tensor:
+        batch, seq_len, _ = x.shape
+        mode = self._plan_mode(x, causal)
+
+        if mode == AttentionMode.SM100_FUSED:
+            context = self._sm100_context(x, valid_token_mask, causal)
+        elif mode in (AttentionMode.EXACT_REFERENCE, AttentionMode.FP32_BASELINE_EXACT):
             q = self._heads_view(self.q_proj(x)).contiguous()
             k = self._heads_view(self.k_proj(x)).contiguous()
             v = self._heads_view(self.v_proj(x)).contiguous()
@@ -149,7 +179,7 @@ class B200FusedSelfAttention(nn.Module):
             context = context.transpose(1, 2).contiguous().view(batch, seq_len, self.d_model)
         else:
             raise NotImplementedError(
-                f"attention mode {plan.mode} runs on the reference's Triton/Gluon (sm_120) stack, "
+                f"attention mode {mode} runs on the reference's Triton/Gluon (sm_120) stack, "
                 "which this package does not ship")
         output = self.out_proj(context)
         if valid_token_mask is not None:

@@ -8,7 +8,17 @@ organiser's (``layers.{i}.norm1/attention/norm2/ffn_in/ffn_out``,
 ``final_norm``), so a state dict moves between the two models unchanged.
 
 Per block: ``x + attention(norm1(x))`` then ``x + ffn_out(gelu(ffn_in(norm2(x))))``,
-padded rows zeroed after each block and after the final LayerNorm.  An optional
+padded rows zeroed after each block and after the final LayerNorm.
+
+With ``fused_epilogues`` (the default) and the attention on its sm_100a path,
+a block runs the elementwise steps inside the fused linear kernel
+(``b200_linear``) where that measured faster than cuBLAS plus the separate
+passes at the end-to-end shapes: ``out_proj`` with its residual add (and the
+padded-row handling), ``ffn_in`` with the exact GELU, and ``ffn_out`` with its
+residual add and padded-row zeroing when a padding mask is given (without a
+mask, ``ffn_out`` is a plain cuBLAS GEMM followed by the add).  The QKV
+projection stays one cuBLAS GEMM.  Every rounding point of the unfused
+sequence is kept.  An optional
 token embedding in front serves the end-to-end configuration (vocabulary 32000,
 uniform random token ids); the reference model itself starts from hidden
 states, so parity is defined from the hidden states onward.
@@ -24,6 +34,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .attention_dispatch import AttentionModelSpec
+from .linear import b200_linear, linear_supported
 from .modules import B200FusedSelfAttention
 
 
@@ -60,8 +71,9 @@ class DecoderBlock(nn.Module):
     def __init__(self, d_model: int, num_heads: int, ffn_dim: int, *,
                  attention_cls: Type[nn.Module] = B200FusedSelfAttention,
                  model_spec: Optional[AttentionModelSpec] = None,
-                 layer_index: Optional[int] = None) -> None:
+                 layer_index: Optional[int] = None, fused_epilogues: bool = True) -> None:
         super().__init__()
+        self.fused_epilogues = fused_epilogues
         self.norm1 = nn.LayerNorm(d_model)
         if model_spec is not None:
             self.attention = attention_cls(d_model, num_heads, model_spec=model_spec,
@@ -74,11 +86,30 @@ class DecoderBlock(nn.Module):
 
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor],
                 causal: bool) -> torch.Tensor:
-        x = x + self.attention(self.norm1(x), valid_token_mask, causal)
+        h = self.norm1(x)
+        if self._fusable(h):
+            fused = self.attention.residual_forward(h, x, valid_token_mask, causal)
+            if fused is not None:
+                return self._fused_ffn(fused, valid_token_mask)
+        x = x + self.attention(h, valid_token_mask, causal)
         x = x + self.ffn_out(F.gelu(self.ffn_in(self.norm2(x)), approximate="none"))
         if valid_token_mask is not None:
             x = x.masked_fill(~valid_token_mask[..., None], 0)
         return x
+
+    def _fusable(self, h: torch.Tensor) -> bool:
+        """The block's linear layers fit the fused kernel for input ``h``."""
+        w = self.ffn_out.weight
+        return (self.fused_epilogues and isinstance(self.attention, B200FusedSelfAttention)
+                and linear_supported(h, self.ffn_in.weight) and w.device == h.device
+                and w.dtype == h.dtype and w.shape[0] % 8 == 0 and w.shape[1] % 8 == 0)
+
+    def _fused_ffn(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
+        h = b200_linear(self.norm2(x), self.ffn_in.weight, self.ffn_in.bias, activation="gelu")
+        if valid_token_mask is None:
+            return x + self.ffn_out(h)
+        return b200_linear(h, self.ffn_out.weight, self.ffn_out.bias, residual=x,
+                           row_mask=valid_token_mask, masked_rows="zero")
 
 
 class Decoder(nn.Module):
@@ -86,7 +117,7 @@ class Decoder(nn.Module):
 
     def __init__(self, config: DecoderConfig, *,
                  attention_cls: Type[nn.Module] = B200FusedSelfAttention,
-                 model_scoped_plans: bool = True) -> None:
+                 model_scoped_plans: bool = True, fused_epilogues: bool = True) -> None:
         super().__init__()
         self.config = config
         spec = config.attention_spec() if model_scoped_plans else None
@@ -94,7 +125,8 @@ class Decoder(nn.Module):
         self.layers = nn.ModuleList([
             DecoderBlock(config.d_model, config.num_heads, config.ffn_dim,
                          attention_cls=attention_cls, model_spec=spec,
-                         layer_index=i if spec is not None else None)
+                         layer_index=i if spec is not None else None,
+                         fused_epilogues=fused_epilogues)
             for i in range(config.num_layers)])
         self.final_norm = nn.LayerNorm(config.d_model)
 

@@ -84,9 +84,22 @@ constexpr int kIssuerSpin = 4096;
 #endif
 // 0: the host picks the tile width per shape; 128 or 256 forces it.
 constexpr int kForceTileN = B200_LINEAR_TILE_N;
+#ifndef B200_LINEAR_CLUSTER_ACQUIRE
+#define B200_LINEAR_CLUSTER_ACQUIRE 0
+#endif
+// Pair kernel: waits on barriers the other CTA (or its loads) completes use
+// cluster-scope acquire (1) or the default CTA scope (0).
+constexpr bool kClusterAcquire = B200_LINEAR_CLUSTER_ACQUIRE != 0;
+#ifndef B200_LINEAR_GROUP_M
+#define B200_LINEAR_GROUP_M 8
+#endif
+// Tile raster: groups of this many row blocks are walked column by column, so
+// the tiles in flight share both x rows and W rows in L2 (0: row by row).
+constexpr int kGroupM = B200_LINEAR_GROUP_M;
 
 struct LinArgs {
   int32_t m, n, k;
+  int32_t num_m_tiles;
   int32_t num_n_tiles;
   int32_t num_tiles;
   int32_t k_blocks;
@@ -99,6 +112,21 @@ struct LinArgs {
   int64_t ld_y;
   int32_t* err;
 };
+
+// Row block and column block of tile t (num_m row blocks, num_n column blocks).
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
+  if (kGroupM > 0) {
+    const int per_group = kGroupM * num_n;
+    const int g = t / per_group;
+    const int rows = min(kGroupM, num_m - g * kGroupM);  // the last group may be shorter
+    const int r = t - g * per_group;
+    tm = g * kGroupM + r % rows;
+    tn = r / rows;
+  } else {
+    tm = t / num_n;
+    tn = t % num_n;
+  }
+}
 
 template <int BN_>
 struct LinCfg {
@@ -131,20 +159,27 @@ struct PairCfg {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = kHalfN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = 6;
-  static constexpr int kOffBar = kStages * kStageBytes;
+  static constexpr int kStages = 5;
+  // Output staging: per epilogue half two buffers of 128 rows x 64 columns
+  // (16-bit, 128-byte swizzle), written by the threads and stored by TMA; with
+  // a residual, TMA first loads the residual block into the same buffer.
+  static constexpr int kOutBlockCols = 64;
+  static constexpr int kOutBufBytes = kBM * kOutBlockCols * 2;
+  static constexpr int kOffOut = kStages * kStageBytes;
+  static constexpr int kOffBar = kOffOut + 4 * kOutBufBytes;
   static constexpr int kBarFull = 0;
   static constexpr int kBarEmpty = kStages;
   static constexpr int kBarAccFull = 2 * kStages;       // [2]
   static constexpr int kBarAccEmpty = 2 * kStages + 2;  // [2]
   static constexpr int kBarDrain = 2 * kStages + 4;
-  static constexpr int kNumBars = kBarDrain + 1;
+  static constexpr int kBarRes = 2 * kStages + 5;       // [half][buffer]
+  static constexpr int kNumBars = kBarRes + 4;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KB per-block shared memory limit");
   static constexpr uint32_t kTmemCols = 2 * BN;
   static constexpr int kHalfCols = BN / 2;
-  static constexpr int kChunks = kHalfCols / 32;
+  static constexpr int kBlocksPerHalf = kHalfCols / kOutBlockCols;
 };
 
 // ---------------------------------------------------------------- helpers
@@ -240,9 +275,76 @@ __device__ __forceinline__ float round16(float x) {
   }
 }
 
+#ifndef B200_LINEAR_GELU_AS
+#define B200_LINEAR_GELU_AS 1
+#endif
+// 1: GELU from the Abramowitz-Stegun erfc formula below, in packed pairs;
+// 0: x * 0.5 * (1 + erff(x / sqrt 2)) with CUDA's erff.
+constexpr bool kGeluAS = B200_LINEAR_GELU_AS != 0;
+
 // Exact GELU in fp32 in the evaluation order x * 0.5 * (1 + erf(x / sqrt 2)).
 __device__ __forceinline__ float gelu_erf(float x) {
   return x * 0.5f * (1.0f + erff(x * 0.70710678118654752440f));
+}
+
+// Packed fp32 pairs (sm_100 .f32x2): each lane rounds like the scalar op.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// GELU of a pair, x * Phi(x) with the normal CDF Phi from the complementary
+// error function: for z = |x| / sqrt 2, Abramowitz & Stegun (Handbook of
+// Mathematical Functions, 7.1.26, after Hastings) give
+//   erfc(z) = (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),  t = 1 / (1 + p z)
+// with absolute error <= 1.5e-7.  q = erfc(z) / 2 = Phi(-|x|), so Phi(x) = q for
+// x < 0 and 1 - q otherwise; taking erfc directly avoids the cancellation of
+// 1 + erf(x / sqrt 2) at negative x.  The coefficients below carry the 1/2.
+__device__ __forceinline__ float2 gelu2_as(float2 x) {
+  constexpr float kInvSqrt2 = 0.70710678118654752f;
+  constexpr float kP = 0.3275911f;
+  const float2 z = make_float2(fabsf(x.x) * kInvSqrt2, fabsf(x.y) * kInvSqrt2);
+  const float2 den = fma2(make_float2(kP, kP), z, make_float2(1.f, 1.f));
+  const float2 t = make_float2(rcp_approx(den.x), rcp_approx(den.y));
+  float2 poly = fma2(make_float2(0.5307027145f, 0.5307027145f), t,
+                     make_float2(-0.7265760135f, -0.7265760135f));
+  poly = fma2(poly, t, make_float2(0.7107068705f, 0.7107068705f));
+  poly = fma2(poly, t, make_float2(-0.142248368f, -0.142248368f));
+  poly = fma2(poly, t, make_float2(0.127414796f, 0.127414796f));
+  poly = mul2(poly, t);
+  const float2 arg = mul2(mul2(z, z), make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  const float2 e = make_float2(ptx::ex2_approx(arg.x), ptx::ex2_approx(arg.y));
+  const float2 q = mul2(poly, e);
+  const float2 phi = make_float2(x.x < 0.f ? q.x : 1.f - q.x, x.y < 0.f ? q.y : 1.f - q.y);
+  return mul2(x, phi);
 }
 
 __device__ __forceinline__ uint4 ld_nc_v4(const uint16_t* p) {
@@ -260,6 +362,37 @@ __device__ __forceinline__ void load_res32(const LinArgs& args, int row, int col
     const int col = col0 + 8 * g;
     r[g] = (row_in && col < args.n) ? ld_nc_v4(rrow + col) : make_uint4(0u, 0u, 0u, 0u);
   }
+}
+
+// Epilogue of 8 consecutive columns of one row: accumulators a[0..7], bias
+// and residual as packed 16-bit words; returns the 8 packed outputs.
+template <bool kBF16, bool kGelu, bool kRes>
+__device__ __forceinline__ uint4 epi8(const uint32_t* a, uint4 bias, uint4 res, bool keep,
+                                      int32_t keep_residual) {
+  const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bias);
+  const uint32_t* rw = reinterpret_cast<const uint32_t*>(&res);
+  uint32_t out[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 acc = make_float2(__uint_as_float(a[2 * j]), __uint_as_float(a[2 * j + 1]));
+    const float2 sum = add2(acc, unpack2<kBF16>(bw[j]));
+    float2 t = make_float2(round16<kBF16>(sum.x), round16<kBF16>(sum.y));
+    if constexpr (kGelu) {
+      if constexpr (kGeluAS) {
+        const float2 g = gelu2_as(t);
+        t = make_float2(round16<kBF16>(g.x), round16<kBF16>(g.y));
+      } else {
+        t = make_float2(round16<kBF16>(gelu_erf(t.x)), round16<kBF16>(gelu_erf(t.y)));
+      }
+    }
+    if constexpr (kRes) {
+      const float2 y = add2(unpack2<kBF16>(rw[j]), t);
+      out[j] = keep ? pack2<kBF16>(y.x, y.y) : (keep_residual ? rw[j] : 0u);
+    } else {
+      out[j] = keep ? pack2<kBF16>(t.x, t.y) : 0u;
+    }
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 // Epilogue of this thread's output row over kChunks x 32 accumulator columns:
@@ -288,35 +421,15 @@ __device__ __forceinline__ void epilogue_row(const LinArgs& args, uint32_t tacc,
     }
     ptx::tmem_wait_ld();
     if (c == kChunks - 1) release();
-    uint4 bias4[4];
+    uint4 outv[4];
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const int col = col0 + 8 * g;
-      bias4[g] = (args.bias && col < N) ? ld_nc_v4(args.bias + col) : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 bias = (args.bias && col < N) ? ld_nc_v4(args.bias + col) : make_uint4(0u, 0u, 0u, 0u);
+      outv[g] = epi8<kBF16, kGelu, kRes>(a + 8 * g, bias, kRes ? rcur[g] : make_uint4(0u, 0u, 0u, 0u),
+                                         keep, args.masked_keep_residual);
     }
-    const uint32_t* bw = reinterpret_cast<const uint32_t*>(bias4);
-    const uint32_t* rw = reinterpret_cast<const uint32_t*>(rcur);
-    uint32_t out[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float2 bv = unpack2<kBF16>(bw[j]);
-      float t0 = round16<kBF16>(__uint_as_float(a[2 * j]) + bv.x);
-      float t1 = round16<kBF16>(__uint_as_float(a[2 * j + 1]) + bv.y);
-      if constexpr (kGelu) {
-        t0 = round16<kBF16>(gelu_erf(t0));
-        t1 = round16<kBF16>(gelu_erf(t1));
-      }
-      if constexpr (kRes) {
-        const float2 rv = unpack2<kBF16>(rw[j]);
-        if (keep) {
-          out[j] = pack2<kBF16>(rv.x + t0, rv.y + t1);
-        } else {
-          out[j] = args.masked_keep_residual ? rw[j] : 0u;
-        }
-      } else {
-        out[j] = keep ? pack2<kBF16>(t0, t1) : 0u;
-      }
-    }
+    const uint32_t* out = reinterpret_cast<const uint32_t*>(outv);
     if (row_in) {
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
@@ -380,8 +493,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t L = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
-        const int m0 = (t / args.num_n_tiles) * kBM;
-        const int n0 = (t % args.num_n_tiles) * BN;
+        int tm, tn;
+        tile_coords(t, args.num_m_tiles, args.num_n_tiles, tm, tn);
+        const int m0 = tm * kBM;
+        const int n0 = tn * BN;
         for (int kb = 0; kb < k_blocks; ++kb) {
           const uint32_t s = L % S, r = L / S;
           if (!issuer_wait(bar(C::kBarEmpty + s), (r & 1u) ^ 1u, abort_flag, args.err)) {
@@ -463,8 +578,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x, ++tc) {
       const int buf = tc & 1;
       const uint32_t use = static_cast<uint32_t>(tc >> 1);
-      const int row = (t / args.num_n_tiles) * kBM + rl;
-      const int cbase = (t % args.num_n_tiles) * BN + half * C::kHalfCols;
+      int tm, tn;
+      tile_coords(t, args.num_m_tiles, args.num_n_tiles, tm, tn);
+      const int row = tm * kBM + rl;
+      const int cbase = tn * BN + half * C::kHalfCols;
       uint4 rnext[4];  // residual of the first chunk, before the accumulator is ready
       if constexpr (kRes) load_res32(args, row, cbase, rnext);
       if (!warp_wait_bar(bar(C::kBarAccFull + buf), use & 1u, abort_flag, args.err)) break;
@@ -491,7 +608,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <bool kBF16, bool kGelu, bool kRes>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     linear_sm100_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
-                             const __grid_constant__ CUtensorMap tm_w, const LinArgs args) {
+                             const __grid_constant__ CUtensorMap tm_w,
+                             const __grid_constant__ CUtensorMap tm_y,
+                             const __grid_constant__ CUtensorMap tm_r, const LinArgs args) {
   using C = PairCfg;
   constexpr int BN = C::BN;
   constexpr int S = C::kStages;
@@ -522,10 +641,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       ptx::mbar_init(bar(C::kBarAccEmpty + b), 2 * kEpiWarps);  // leader: both CTAs' warps
     }
     ptx::mbar_init(bar(C::kBarDrain), 1);
+    for (int b = 0; b < 4; ++b) ptx::mbar_init(bar(C::kBarRes + b), 1);
     ptx::fence_mbar_init();
     ptx::fence_proxy_async_smem();
     ptx::tma_prefetch_desc(&tm_x);
     ptx::tma_prefetch_desc(&tm_w);
+    ptx::tma_prefetch_desc(&tm_y);
+    if (kRes) ptx::tma_prefetch_desc(&tm_r);
   }
   if (warp == kMmaWarp) {
     ptx::tmem_alloc_pair(sbase + C::kOffMisc, C::kTmemCols);
@@ -544,11 +666,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t L = 0;
       bool ok = true;
       for (int t = pair; ok && t < args.num_tiles; t += num_pairs) {
-        const int m0 = (t / args.num_n_tiles) * (2 * kBM) + static_cast<int>(rank) * kBM;
-        const int n0 = (t % args.num_n_tiles) * BN + static_cast<int>(rank) * C::kHalfN;
+        int tm, tn;
+        tile_coords(t, args.num_m_tiles, args.num_n_tiles, tm, tn);
+        const int m0 = tm * (2 * kBM) + static_cast<int>(rank) * kBM;
+        const int n0 = tn * BN + static_cast<int>(rank) * C::kHalfN;
         for (int kb = 0; kb < k_blocks; ++kb) {
           const uint32_t s = L % S, r = L / S;
-          if (!issuer_wait<true>(bar(C::kBarEmpty + s), (r & 1u) ^ 1u, abort_flag, args.err)) {
+          if (!issuer_wait<kClusterAcquire>(bar(C::kBarEmpty + s), (r & 1u) ^ 1u, abort_flag, args.err)) {
             ok = false;
             break;
           }
@@ -564,7 +688,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const uint32_t first = L > static_cast<uint32_t>(S) ? L - S : 0u;
         for (uint32_t x = first; x < L; ++x) {
           const uint64_t t0 = ptx::globaltimer_ns();
-          while (!ptx::mbar_try_wait_cluster(bar(C::kBarFull + x % S), (x / S) & 1u) &&
+          while (!try_wait<kClusterAcquire>(bar(C::kBarFull + x % S), (x / S) & 1u) &&
                  ptx::globaltimer_ns() - t0 < kWaitTimeoutNs) {
           }
         }
@@ -584,7 +708,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int buf = tc & 1;
         const uint32_t use = static_cast<uint32_t>(tc >> 1);
         // both CTAs' epilogues have read this accumulator's previous tile
-        if (!issuer_wait<true>(bar(C::kBarAccEmpty + buf), (use & 1u) ^ 1u, abort_flag, args.err)) {
+        if (!issuer_wait<kClusterAcquire>(bar(C::kBarAccEmpty + buf), (use & 1u) ^ 1u, abort_flag, args.err)) {
           ok = false;
           break;
         }
@@ -592,7 +716,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const uint32_t acc = tmem + static_cast<uint32_t>(buf * BN);
         for (int kb = 0; kb < k_blocks; ++kb) {
           const uint32_t s = L % S, r = L / S;
-          if (!issuer_wait<true>(bar(C::kBarFull + s), r & 1u, abort_flag, args.err)) {
+          if (!issuer_wait<kClusterAcquire>(bar(C::kBarFull + s), r & 1u, abort_flag, args.err)) {
             ok = false;
             break;
           }
@@ -620,29 +744,101 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
+    // Each half (4 warps, 128 threads = 128 rows) writes its 128 columns as two
+    // 64-column blocks, block b through staging buffer b of the half; one
+    // elected thread per half loads the tile's residual blocks (before the
+    // accumulator is ready) and issues the output stores.
     const int e = warp - kEpiWarp0;
     const int quad = warp & 3;
     const int half = e >> 2;
     const int rl = quad * 32 + lane;
+    const bool elected = (e & 3) == 0 && lane == 0;
+    const uint32_t named = 1u + static_cast<uint32_t>(half);  // named barrier of the half
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t acc_empty_leader = ptx::mapa_shared(bar(C::kBarAccEmpty), 0);
+    const uint32_t out0 = sbase + C::kOffOut + static_cast<uint32_t>(half * 2 * C::kOutBufBytes);
+    static_assert(C::kBlocksPerHalf == 2, "one staging buffer per block of the tile");
     int tc = 0;
     for (int t = pair; t < args.num_tiles; t += num_pairs, ++tc) {
       const int buf = tc & 1;
       const uint32_t use = static_cast<uint32_t>(tc >> 1);
-      const int row = (t / args.num_n_tiles) * (2 * kBM) + static_cast<int>(rank) * kBM + rl;
-      const int cbase = (t % args.num_n_tiles) * BN + half * C::kHalfCols;
-      uint4 rnext[4];
-      if constexpr (kRes) load_res32(args, row, cbase, rnext);
-      if (!warp_wait_bar<true>(bar(C::kBarAccFull + buf), use & 1u, abort_flag, args.err)) break;
+      int tm, tn;
+      tile_coords(t, args.num_m_tiles, args.num_n_tiles, tm, tn);
+      const int row0 = tm * (2 * kBM) + static_cast<int>(rank) * kBM;
+      const int row = row0 + rl;
+      const int cbase = tn * BN + half * C::kHalfCols;
+      if (elected) {
+        // the previous tile's stores have read both buffers: refill them
+        ptx::bulk_wait_group_read_all();
+        if constexpr (kRes) {
+#pragma unroll
+          for (int b = 0; b < C::kBlocksPerHalf; ++b) {
+            const uint32_t rb = bar(C::kBarRes + half * 2 + b);
+            ptx::mbar_arrive_expect_tx(rb, C::kOutBufBytes);
+            ptx::tma_load_2d(out0 + b * C::kOutBufBytes, &tm_r, rb, cbase + b * C::kOutBlockCols,
+                             row0);
+          }
+        }
+      }
+      bool keep = true;
+      if (args.row_mask && row < args.m) keep = args.row_mask[row] != 0;
+      // the four warps of the half agree before any of them passes a named
+      // barrier (this one also orders the buffer refill above before any write)
+      const bool acc_ok =
+          warp_wait_bar<kClusterAcquire>(bar(C::kBarAccFull + buf), use & 1u, abort_flag, args.err);
+      if (!ptx::named_barrier_and(named, 128, acc_ok)) break;
       ptx::tc_fence_after();
       const uint32_t tacc = tmem + lane_off + static_cast<uint32_t>(buf * BN + half * C::kHalfCols);
-      epilogue_row<C::kChunks, kBF16, kGelu, kRes>(args, tacc, row, cbase, rnext, [&] {
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive_cluster(acc_empty_leader + 8u * buf);
-      });
+      bool ok = true;
+#pragma unroll 1
+      for (int b = 0; b < C::kBlocksPerHalf; ++b) {
+        const uint32_t stage = out0 + b * C::kOutBufBytes;
+        const int col0 = cbase + b * C::kOutBlockCols;
+        uint32_t a0[32], a1[32];
+        ptx::tmem_ld_32x32b_x32(tacc + b * C::kOutBlockCols, a0);
+        ptx::tmem_ld_32x32b_x32(tacc + b * C::kOutBlockCols + 32, a1);
+        ptx::tmem_wait_ld();
+        if (b == C::kBlocksPerHalf - 1) {
+          // this warp's last read of the accumulator: hand it back to the issuer
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive_cluster(acc_empty_leader + 8u * buf);
+        }
+        bool res_ok = true;
+        if constexpr (kRes)
+          res_ok = warp_wait_bar(bar(C::kBarRes + half * 2 + b), static_cast<uint32_t>(tc) & 1u,
+                                 abort_flag, args.err);
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          const int col = col0 + 8 * g;
+          const uint32_t addr = stage + static_cast<uint32_t>(rl * 128) +
+                                ((static_cast<uint32_t>(g) ^ static_cast<uint32_t>(rl & 7)) << 4);
+          uint4 res = make_uint4(0u, 0u, 0u, 0u);
+          if constexpr (kRes) {
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(res.x), "=r"(res.y), "=r"(res.z), "=r"(res.w)
+                         : "r"(addr));
+          }
+          const uint4 bias =
+              (args.bias && col < args.n) ? ld_nc_v4(args.bias + col) : make_uint4(0u, 0u, 0u, 0u);
+          const uint32_t* src = g < 4 ? a0 + 8 * g : a1 + 8 * (g - 4);
+          const uint4 o = epi8<kBF16, kGelu, kRes>(src, bias, res, keep, args.masked_keep_residual);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(o.x), "r"(o.y),
+                       "r"(o.z), "r"(o.w)
+                       : "memory");
+        }
+        ptx::fence_proxy_async_smem();
+        // the block is in shared memory (unless a residual load never arrived)
+        ok = ptx::named_barrier_and(named, 128, res_ok);
+        if (!ok) break;
+        if (elected) {
+          ptx::tma_store_2d(&tm_y, stage, col0, row0);
+          ptx::bulk_commit_group();
+        }
+      }
+      if (!ok) break;
     }
+    if (elected) ptx::bulk_wait_group_all();  // stores complete before the CTA ends
   }
 
   ptx::tc_fence_before();
@@ -755,8 +951,9 @@ int launch(const CUtensorMap& mx, const CUtensorMap& mw, const LinArgs& a, int d
 }
 
 template <bool BF, bool G, bool R>
-int launch_pair(const CUtensorMap& mx, const CUtensorMap& mw, const LinArgs& a, int dev,
-                int num_sms, cudaStream_t stream) {
+int launch_pair(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& my,
+                const CUtensorMap& mr, const LinArgs& a, int dev, int num_sms,
+                cudaStream_t stream) {
   auto kernel = linear_sm100_pair_kernel<BF, G, R>;
   static std::once_flag once[kMaxDevices];
   static cudaError_t attr_err[kMaxDevices];
@@ -780,7 +977,7 @@ int launch_pair(const CUtensorMap& mx, const CUtensorMap& mw, const LinArgs& a, 
     return B200_ATTN_ERR_LAUNCH;
   }
   const int pairs = a.num_tiles < max_pairs[dev] ? a.num_tiles : max_pairs[dev];
-  kernel<<<2 * pairs, kThreads, PairCfg::kSmemBytes, stream>>>(mx, mw, a);
+  kernel<<<2 * pairs, kThreads, PairCfg::kSmemBytes, stream>>>(mx, mw, my, mr, a);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(cudaGetErrorString(e));
@@ -789,21 +986,22 @@ int launch_pair(const CUtensorMap& mx, const CUtensorMap& mw, const LinArgs& a, 
   return B200_ATTN_OK;
 }
 
-int dispatch_pair(const CUtensorMap& mx, const CUtensorMap& mw, const LinArgs& a,
-                  const b200_linear_params* p, int dev, int num_sms, cudaStream_t s) {
+int dispatch_pair(const CUtensorMap* maps, const LinArgs& a, const b200_linear_params* p, int dev,
+                  int num_sms, cudaStream_t s) {
   const bool bf = p->dtype == B200_ATTN_DTYPE_BF16;
   const bool g = p->activation == B200_LINEAR_ACT_GELU;
   const bool r = p->residual != nullptr;
+  const CUtensorMap &mx = maps[0], &mw = maps[1], &my = maps[2], &mr = maps[3];
   if (bf) {
-    if (g) return r ? launch_pair<true, true, true>(mx, mw, a, dev, num_sms, s)
-                    : launch_pair<true, true, false>(mx, mw, a, dev, num_sms, s);
-    return r ? launch_pair<true, false, true>(mx, mw, a, dev, num_sms, s)
-             : launch_pair<true, false, false>(mx, mw, a, dev, num_sms, s);
+    if (g) return r ? launch_pair<true, true, true>(mx, mw, my, mr, a, dev, num_sms, s)
+                    : launch_pair<true, true, false>(mx, mw, my, mr, a, dev, num_sms, s);
+    return r ? launch_pair<true, false, true>(mx, mw, my, mr, a, dev, num_sms, s)
+             : launch_pair<true, false, false>(mx, mw, my, mr, a, dev, num_sms, s);
   }
-  if (g) return r ? launch_pair<false, true, true>(mx, mw, a, dev, num_sms, s)
-                  : launch_pair<false, true, false>(mx, mw, a, dev, num_sms, s);
-  return r ? launch_pair<false, false, true>(mx, mw, a, dev, num_sms, s)
-           : launch_pair<false, false, false>(mx, mw, a, dev, num_sms, s);
+  if (g) return r ? launch_pair<false, true, true>(mx, mw, my, mr, a, dev, num_sms, s)
+                  : launch_pair<false, true, false>(mx, mw, my, mr, a, dev, num_sms, s);
+  return r ? launch_pair<false, false, true>(mx, mw, my, mr, a, dev, num_sms, s)
+           : launch_pair<false, false, false>(mx, mw, my, mr, a, dev, num_sms, s);
 }
 
 template <int BN>
@@ -916,7 +1114,8 @@ extern "C" int32_t b200_linear_fwd(const b200_linear_params* p, void* stream) {
   a.n = static_cast<int32_t>(p->n);
   a.k = static_cast<int32_t>(p->k);
   a.num_n_tiles = static_cast<int32_t>(ceil_div(p->n, bn));
-  a.num_tiles = static_cast<int32_t>(ceil_div(p->m, pair ? 2 * kBM : kBM) * a.num_n_tiles);
+  a.num_m_tiles = static_cast<int32_t>(ceil_div(p->m, pair ? 2 * kBM : kBM));
+  a.num_tiles = a.num_m_tiles * a.num_n_tiles;
   a.k_blocks = static_cast<int32_t>(ceil_div(p->k, kBK));
   a.bias = static_cast<const uint16_t*>(p->bias);
   a.residual = static_cast<const uint16_t*>(p->residual);
@@ -927,7 +1126,20 @@ extern "C" int32_t b200_linear_fwd(const b200_linear_params* p, void* stream) {
   a.ld_y = p->y_row_stride;
   a.err = p->error_word;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (pair) return dispatch_pair(mx, mw, a, p, dev, g_dev[dev].num_sms, s);
+  if (pair) {
+    // the output (and the residual) leave and enter through 64 x 128 TMA boxes
+    CUtensorMap maps[4] = {mx, mw, {}, {}};
+    if ((rc = encode_rows(&maps[2], p->y, p->m, p->n, p->y_row_stride, kBM, bf)) != B200_ATTN_OK)
+      return rc;
+    if (p->residual) {
+      if ((rc = encode_rows(&maps[3], p->residual, p->m, p->n, p->residual_row_stride, kBM, bf)) !=
+          B200_ATTN_OK)
+        return rc;
+    } else {
+      maps[3] = maps[2];
+    }
+    return dispatch_pair(maps, a, p, dev, g_dev[dev].num_sms, s);
+  }
   const int grid = static_cast<int>(
       a.num_tiles < g_dev[dev].num_sms ? a.num_tiles : g_dev[dev].num_sms);
   return bn == 256 ? dispatch<256>(mx, mw, a, p, dev, grid, s)

@@ -1,0 +1,67 @@
+"""The decoder block with its linear layers on the fused kernel (out_proj +
+residual, ffn_in + GELU, ffn_out + residual + padded-row zeroing) against the
+same weights with cuBLAS linear layers and separate elementwise passes.
+
+Both runs keep every rounding point of the unfused sequence, so they differ
+only by the GEMMs' fp32 summation order; the repository's parity tolerance
+(max-abs <= 2e-2, mean-abs <= 2e-3) applies, and padded rows must be exactly
+zero after every block.
+"""
+
+import pytest
+import torch
+
+from b200_attention import linear as linear_mod
+from b200_attention.transformer import Decoder, DecoderConfig, init_normal_
+from parity import MAX_ABS, MEAN_ABS, compare
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0)
+CFG = DecoderConfig(2, 512, 1024, 16, 4096, 2, True)
+
+
+def _pair(cfg):
+    fused = init_normal_(Decoder(cfg), seed=7).to(device=DEV, dtype=torch.bfloat16).eval()
+    plain = Decoder(cfg, fused_epilogues=False).to(device=DEV, dtype=torch.bfloat16).eval()
+    plain.load_state_dict(fused.state_dict())
+    return fused, plain
+
+
+@pytest.mark.parametrize("padded", [False, True])
+def test_fused_blocks_match_unfused(padded, monkeypatch):
+    fused, plain = _pair(CFG)
+    gen = torch.Generator().manual_seed(11)
+    x = torch.randn(CFG.batch_size, CFG.seq_len, CFG.d_model, generator=gen).to(DEV, torch.bfloat16)
+    mask = None
+    if padded:
+        lengths = torch.tensor([CFG.seq_len, CFG.seq_len // 3])
+        mask = (torch.arange(CFG.seq_len)[None, :] < lengths[:, None]).to(DEV)
+        x = x.masked_fill(~mask[..., None], 0)
+    calls = []
+    real = linear_mod.b200_linear
+
+    def counting(*args, **kwargs):
+        calls.append(kwargs.get("activation"))
+        return real(*args, **kwargs)
+
+    monkeypatch.setattr("b200_attention.transformer.b200_linear", counting)
+    monkeypatch.setattr("b200_attention.modules.b200_linear", counting)
+    with torch.inference_mode():
+        out = fused(x, mask)
+        ref = plain(x, mask)
+    torch.cuda.synchronize()
+    # per block: out_proj (+residual), ffn_in (+GELU), and ffn_out when masked
+    assert len(calls) == CFG.num_layers * (3 if padded else 2)
+    stats = compare(out, ref)
+    assert stats["max_abs"] <= MAX_ABS and stats["mean_abs"] <= MEAN_ABS, stats
+    if mask is not None:
+        assert torch.equal(out[~mask], torch.zeros_like(out[~mask]))
+
+
+def test_autograd_takes_the_unfused_path():
+    fused, plain = _pair(DecoderConfig(1, 256, 1024, 16, 4096, 1, True))
+    x = torch.randn(1, 256, 1024, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    out = fused(x)
+    out.float().sum().backward()
+    assert x.grad is not None and torch.isfinite(x.grad.float()).all()
