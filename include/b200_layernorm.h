@@ -1,0 +1,53 @@
+/*
+ * b200_layernorm.h — C ABI of the LayerNorm that runs between the block's
+ * linear layers.
+ *
+ * Semantics of nn.LayerNorm over the last dimension (the block's norm1 and
+ * norm2, torch_transformer_benchmark.py:129-131, 141-142, and the model's
+ * final_norm, :161, :170):
+ *   y = (x - mean(x)) / sqrt(var(x) + eps) * weight + bias
+ * with the biased variance; mean, variance and the affine step in fp32, the
+ * result rounded once to the element type.
+ *
+ * x and y are row-major [rows, cols] with a contiguous last dimension (row
+ * strides in ELEMENTS); weight and bias are [cols] or NULL (1 and 0).  Element
+ * types are B200_ATTN_DTYPE_* (b200_attn.h); return codes are B200_ATTN_*.
+ */
+#ifndef B200_LAYERNORM_H_
+#define B200_LAYERNORM_H_
+
+#include "b200_attn.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct b200_layernorm_params {
+  const void* x;          /* [rows, cols] */
+  const void* weight;     /* [cols] or NULL */
+  const void* bias;       /* [cols] or NULL */
+  void* y;                /* [rows, cols], may be x itself */
+  int64_t rows;
+  int64_t cols;           /* multiple of 8, at most 4096 */
+  int64_t x_row_stride;   /* elements */
+  int64_t y_row_stride;
+  float eps;              /* > 0 */
+  int32_t dtype;          /* B200_ATTN_DTYPE_* */
+} b200_layernorm_params;
+
+/* Host-only validation (sizes, dtype, eps, 16-byte alignment of bases and row
+ * strides).  Makes no CUDA call.  Replaces the shape checks of
+ * torch.nn.functional.layer_norm for these calls. */
+B200_ATTN_API int32_t b200_layernorm_check(const b200_layernorm_params* p);
+
+/* Launch the LayerNorm on `stream` (NULL = legacy default stream): one kernel,
+ * no allocation, no synchronisation; the caller's current device is left as it
+ * was.  Replaces nn.LayerNorm's forward in the reference block
+ * (torch_transformer_benchmark.py:141-142, 170). */
+B200_ATTN_API int32_t b200_layernorm_fwd(const b200_layernorm_params* p, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_LAYERNORM_H_ */

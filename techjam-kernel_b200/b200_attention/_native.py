@@ -1,4 +1,5 @@
-"""ctypes binding of the C ABI in ``include/b200_attn.h`` and ``include/b200_linear.h``.
+"""ctypes binding of the C ABI in ``include/b200_attn.h``, ``include/b200_linear.h``
+and ``include/b200_layernorm.h``.
 
 This module is torch-free: it loads ``libb200_attention.so`` and describes the
 parameter struct.  The library is loaded from this directory only; a missing or
@@ -43,6 +44,12 @@ LINEAR_SYMBOLS = (
     "b200_linear_check",
     "b200_linear_fwd",
     "b200_linear_tile_n",
+)
+
+# Every symbol ``include/b200_layernorm.h`` declares.
+LAYERNORM_SYMBOLS = (
+    "b200_layernorm_check",
+    "b200_layernorm_fwd",
 )
 
 LINEAR_ACT_NONE = 0
@@ -102,6 +109,23 @@ class LinearParams(ctypes.Structure):
     ]
 
 
+class LayerNormParams(ctypes.Structure):
+    """Mirror of ``b200_layernorm_params``."""
+
+    _fields_ = [
+        ("x", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("y", ctypes.c_void_p),
+        ("rows", ctypes.c_int64),
+        ("cols", ctypes.c_int64),
+        ("x_row_stride", ctypes.c_int64),
+        ("y_row_stride", ctypes.c_int64),
+        ("eps", ctypes.c_float),
+        ("dtype", ctypes.c_int32),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -131,6 +155,10 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.b200_linear_fwd.argtypes = [ctypes.POINTER(LinearParams), ctypes.c_void_p]
     lib.b200_linear_tile_n.restype = ctypes.c_int32
     lib.b200_linear_tile_n.argtypes = [ctypes.POINTER(LinearParams), ctypes.c_int32]
+    lib.b200_layernorm_check.restype = ctypes.c_int32
+    lib.b200_layernorm_check.argtypes = [ctypes.POINTER(LayerNormParams)]
+    lib.b200_layernorm_fwd.restype = ctypes.c_int32
+    lib.b200_layernorm_fwd.argtypes = [ctypes.POINTER(LayerNormParams), ctypes.c_void_p]
     return lib
 
 

@@ -1,0 +1,92 @@
+"""LayerNorm over the last dimension on the B200 (``include/b200_layernorm.h``).
+
+``b200_layer_norm(x, weight, bias, eps)`` has the semantics of
+``F.layer_norm(x, (x.shape[-1],), weight, bias, eps)`` (biased variance; mean,
+variance and the affine step in fp32, one rounding to the element type) for
+bf16/fp16 inputs whose last dimension is a multiple of 8 up to 4096.  It
+replaces the reference block's norm1/norm2 and the model's final norm
+(torch_transformer_benchmark.py:141-142, 170) in the decoder's fused path.
+Inference only; anything outside the envelope raises ``ValueError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _native
+from .fused_attention import SUPPORTED_DTYPES
+
+MAX_COLS = 4096
+
+
+def layer_norm_supported(x: torch.Tensor, weight: Optional[torch.Tensor]) -> bool:
+    cols = x.shape[-1]
+    return (x.is_cuda and x.dtype in SUPPORTED_DTYPES and cols % 8 == 0 and 0 < cols <= MAX_COLS
+            and (weight is None or (weight.dtype == x.dtype and weight.device == x.device)))
+
+
+def _rows(t: torch.Tensor, cols: int) -> torch.Tensor:
+    flat = t.reshape(-1, cols)
+    if (flat.stride(-1) != 1 or (flat.shape[0] > 1 and flat.stride(0) % 8 != 0)
+            or flat.data_ptr() % 16 != 0):
+        flat = flat.contiguous()
+    return flat
+
+
+def _vector(t: Optional[torch.Tensor], cols: int, name: str, x: torch.Tensor):
+    if t is None:
+        return None
+    if tuple(t.shape) != (cols,):
+        raise ValueError(f"{name} must have shape ({cols},)")
+    if t.dtype != x.dtype:
+        raise TypeError(f"{name} must have x's dtype {x.dtype}, got {t.dtype}")
+    if t.device != x.device:
+        raise ValueError(f"{name} must be on x's device")
+    if not t.is_contiguous() or t.data_ptr() % 16 != 0:
+        t = t.clone(memory_format=torch.contiguous_format)
+    return t
+
+
+def b200_layer_norm(x: torch.Tensor, weight: Optional[torch.Tensor] = None,
+                    bias: Optional[torch.Tensor] = None, eps: float = 1e-5) -> torch.Tensor:
+    """LayerNorm of ``x`` over its last dimension; a new tensor like ``x``."""
+    if x.dim() < 1:
+        raise ValueError("x must have at least one dimension")
+    cols = x.shape[-1]
+    if x.dtype not in SUPPORTED_DTYPES:
+        raise ValueError(f"b200_layer_norm supports bfloat16 and float16, got {x.dtype}")
+    if cols % 8 or cols > MAX_COLS or cols == 0:
+        raise ValueError(f"b200_layer_norm needs a last dimension that is a multiple of 8 up to "
+                         f"{MAX_COLS}, got {cols}")
+    if not eps > 0:
+        raise ValueError("eps must be positive")
+    w = _vector(weight, cols, "weight", x)
+    b = _vector(bias, cols, "bias", x)
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (x, weight, bias)):
+        raise ValueError("b200_layer_norm is inference-only: it records no autograd graph")
+    if not x.is_cuda:
+        raise ValueError("b200_layer_norm runs on CUDA tensors only")
+    y = torch.empty_like(x, memory_format=torch.contiguous_format)
+    if y.numel() == 0:
+        return y
+    x2 = _rows(x, cols)
+    y2 = y.view(-1, cols)
+    p = _native.LayerNormParams()
+    p.x, p.y = x2.data_ptr(), y2.data_ptr()
+    p.weight = w.data_ptr() if w is not None else None
+    p.bias = b.data_ptr() if b is not None else None
+    p.rows, p.cols = x2.shape[0], cols
+    p.x_row_stride, p.y_row_stride = x2.stride(0), y2.stride(0)
+    p.eps = float(eps)
+    p.dtype = SUPPORTED_DTYPES[x.dtype]
+    lib = _native.load_library()
+    rc = lib.b200_layernorm_fwd(ctypes.byref(p),
+                                ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream))
+    if rc in (_native.ERR_INVALID_ARGUMENT, _native.ERR_ALIGNMENT, _native.ERR_UNSUPPORTED):
+        raise ValueError(f"b200_layernorm_fwd: {_native.error_text(rc)}")
+    if rc != _native.OK:
+        raise RuntimeError(f"b200_layernorm_fwd: {_native.error_text(rc)}")
+    return y

@@ -11,14 +11,15 @@ Per block: ``x + attention(norm1(x))`` then ``x + ffn_out(gelu(ffn_in(norm2(x)))
 padded rows zeroed after each block and after the final LayerNorm.
 
 With ``fused_epilogues`` (the default) and the attention on its sm_100a path,
-a block runs the elementwise steps inside the fused linear kernel
-(``b200_linear``) where that measured faster than cuBLAS plus the separate
-passes at the end-to-end shapes: ``out_proj`` with its residual add (and the
-padded-row handling), ``ffn_in`` with the exact GELU, and ``ffn_out`` with its
-residual add and padded-row zeroing when a padding mask is given (without a
-mask, ``ffn_out`` is a plain cuBLAS GEMM followed by the add).  The QKV
-projection stays one cuBLAS GEMM.  Every rounding point of the unfused
-sequence is kept.  An optional
+a block runs its LayerNorms on the B200 LayerNorm kernel (``b200_layer_norm``)
+and the elementwise steps inside the fused linear kernel (``b200_linear``)
+where that measured faster than cuBLAS plus the separate passes at the
+end-to-end shapes: ``out_proj`` with its residual add (and the padded-row
+handling), ``ffn_in`` with the exact GELU, and ``ffn_out`` with its residual
+add and padded-row zeroing when a padding mask is given (without a mask,
+``ffn_out`` is a plain cuBLAS GEMM followed by the add).  The QKV projection
+stays one cuBLAS GEMM.  Every rounding point of the unfused sequence is kept.
+An optional
 token embedding in front serves the end-to-end configuration (vocabulary 32000,
 uniform random token ids); the reference model itself starts from hidden
 states, so parity is defined from the hidden states onward.
@@ -34,6 +35,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .attention_dispatch import AttentionModelSpec
+from .layernorm import b200_layer_norm, layer_norm_supported
 from .linear import b200_linear, linear_supported
 from .modules import B200FusedSelfAttention
 
@@ -86,26 +88,35 @@ class DecoderBlock(nn.Module):
 
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor],
                 causal: bool) -> torch.Tensor:
-        h = self.norm1(x)
-        if self._fusable(h):
+        if self._fusable(x):
+            h = b200_layer_norm(x, self.norm1.weight, self.norm1.bias, self.norm1.eps)
             fused = self.attention.residual_forward(h, x, valid_token_mask, causal)
             if fused is not None:
                 return self._fused_ffn(fused, valid_token_mask)
-        x = x + self.attention(h, valid_token_mask, causal)
+        x = x + self.attention(self.norm1(x), valid_token_mask, causal)
         x = x + self.ffn_out(F.gelu(self.ffn_in(self.norm2(x)), approximate="none"))
         if valid_token_mask is not None:
             x = x.masked_fill(~valid_token_mask[..., None], 0)
         return x
 
-    def _fusable(self, h: torch.Tensor) -> bool:
-        """The block's linear layers fit the fused kernel for input ``h``."""
+    def _fusable(self, x: torch.Tensor) -> bool:
+        """The block's LayerNorms and linear layers fit the fused kernels for
+        input ``x`` (inference on 16-bit CUDA tensors, sizes multiples of 8)."""
+        if not self.fused_epilogues or not isinstance(self.attention, B200FusedSelfAttention):
+            return False
+        if torch.is_grad_enabled() and (x.requires_grad or
+                                        any(p.requires_grad for p in self.parameters())):
+            return False
         w = self.ffn_out.weight
-        return (self.fused_epilogues and isinstance(self.attention, B200FusedSelfAttention)
-                and linear_supported(h, self.ffn_in.weight) and w.device == h.device
-                and w.dtype == h.dtype and w.shape[0] % 8 == 0 and w.shape[1] % 8 == 0)
+        return (linear_supported(x, self.ffn_in.weight)
+                and layer_norm_supported(x, self.norm1.weight)
+                and layer_norm_supported(x, self.norm2.weight)
+                and w.device == x.device and w.dtype == x.dtype
+                and w.shape[0] % 8 == 0 and w.shape[1] % 8 == 0)
 
     def _fused_ffn(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
-        h = b200_linear(self.norm2(x), self.ffn_in.weight, self.ffn_in.bias, activation="gelu")
+        h = b200_layer_norm(x, self.norm2.weight, self.norm2.bias, self.norm2.eps)
+        h = b200_linear(h, self.ffn_in.weight, self.ffn_in.bias, activation="gelu")
         if valid_token_mask is None:
             return x + self.ffn_out(h)
         return b200_linear(h, self.ffn_out.weight, self.ffn_out.bias, residual=x,
@@ -136,9 +147,14 @@ class Decoder(nn.Module):
         model has an embedding."""
         if self.embed is not None and not torch.is_floating_point(x):
             x = self.embed(x)
+        fused = len(self.layers) > 0 and self.layers[0]._fusable(x)
         for layer in self.layers:
             x = layer(x, valid_token_mask, self.config.causal)
-        x = self.final_norm(x)
+        if fused and layer_norm_supported(x, self.final_norm.weight):
+            x = b200_layer_norm(x, self.final_norm.weight, self.final_norm.bias,
+                                self.final_norm.eps)
+        else:
+            x = self.final_norm(x)
         if valid_token_mask is not None:
             x = x.masked_fill(~valid_token_mask[..., None], 0)
         return x

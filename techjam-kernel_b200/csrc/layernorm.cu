@@ -1,0 +1,212 @@
+// layernorm.cu — LayerNorm over the last dimension of the block's 16-bit
+// activations (the reference block's norm1 / norm2 and the final norm,
+// torch_transformer_benchmark.py:141-142, 170):
+//   y = (x - mean) * rsqrt(var + eps) * weight + bias
+// mean and biased variance in fp32 (two passes over the row held in
+// registers), the affine step in fp32, one rounding to the element type.
+//
+// HBM-bound: one warp per row, 16-byte loads and stores (a warp reads and
+// writes whole contiguous 512-byte segments), the row kept in registers
+// between the mean and variance reductions, so every byte of x is read once
+// and every byte of y written once.  Eight rows per 256-thread block.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <mutex>
+
+#include "b200_layernorm.h"
+
+namespace b200attn {
+// Records the text b200_attn_last_error_detail returns (attn_fwd_sm100.cu).
+void set_error(const char* msg);
+}  // namespace b200attn
+
+namespace b200ln {
+
+using b200attn::set_error;
+
+constexpr int kRowsPerBlock = 8;
+constexpr int kThreads = 32 * kRowsPerBlock;
+constexpr int kMaxCols = 4096;  // the row stays in registers (16 vectors per lane)
+
+struct LnArgs {
+  const uint16_t* x;
+  const uint16_t* w;
+  const uint16_t* b;
+  uint16_t* y;
+  int64_t rows, ldx, ldy;
+  int32_t cols;
+  float eps;
+};
+
+template <bool BF16>
+__device__ __forceinline__ float2 unpack2(uint32_t v) {
+  if constexpr (BF16) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+  } else {
+    __half2 h = *reinterpret_cast<__half2*>(&v);
+    return __half22float2(h);
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (BF16) {
+    __nv_bfloat162 r = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&r);
+  } else {
+    __half2 r = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// VPL: 16-byte vectors per lane (8 elements each), cols <= 256 * VPL.
+template <int VPL, bool BF16>
+__global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + warp;
+  if (row >= a.rows) return;
+  const uint16_t* xr = a.x + row * a.ldx;
+  uint4 v[VPL];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int col = (i * 32 + lane) * 8;
+    v[i] = col < a.cols ? __ldg(reinterpret_cast<const uint4*>(xr + col)) : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack2<BF16>(w[j]);
+      s += f.x + f.y;
+    }
+  }
+  const float inv_n = 1.f / static_cast<float>(a.cols);
+  const float mean = warp_sum(s) * inv_n;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int col = (i * 32 + lane) * 8;
+    if (col >= a.cols) continue;  // padding lanes hold zeros, not x - mean
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack2<BF16>(w[j]);
+      const float d0 = f.x - mean, d1 = f.y - mean;
+      q = fmaf(d0, d0, q);
+      q = fmaf(d1, d1, q);
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) * inv_n + a.eps);
+  uint16_t* yr = a.y + row * a.ldy;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int col = (i * 32 + lane) * 8;
+    if (col >= a.cols) continue;
+    const uint4 g4 = a.w ? __ldg(reinterpret_cast<const uint4*>(a.w + col)) : make_uint4(0u, 0u, 0u, 0u);
+    const uint4 b4 = a.b ? __ldg(reinterpret_cast<const uint4*>(a.b + col)) : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[i]);
+    const uint32_t* gw = reinterpret_cast<const uint32_t*>(&g4);
+    const uint32_t* bw = reinterpret_cast<const uint32_t*>(&b4);
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack2<BF16>(w[j]);
+      const float2 g = a.w ? unpack2<BF16>(gw[j]) : make_float2(1.f, 1.f);
+      const float2 bb = a.b ? unpack2<BF16>(bw[j]) : make_float2(0.f, 0.f);
+      o[j] = pack2<BF16>(fmaf((f.x - mean) * rstd, g.x, bb.x), fmaf((f.y - mean) * rstd, g.y, bb.y));
+    }
+    *reinterpret_cast<uint4*>(yr + col) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <bool BF>
+int launch(const LnArgs& a, cudaStream_t s) {
+  const unsigned grid = static_cast<unsigned>((a.rows + kRowsPerBlock - 1) / kRowsPerBlock);
+  const int vpl = (a.cols + 255) / 256;
+  if (vpl <= 1) layernorm_kernel<1, BF><<<grid, kThreads, 0, s>>>(a);
+  else if (vpl <= 2) layernorm_kernel<2, BF><<<grid, kThreads, 0, s>>>(a);
+  else if (vpl <= 4) layernorm_kernel<4, BF><<<grid, kThreads, 0, s>>>(a);
+  else if (vpl <= 8) layernorm_kernel<8, BF><<<grid, kThreads, 0, s>>>(a);
+  else layernorm_kernel<16, BF><<<grid, kThreads, 0, s>>>(a);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(cudaGetErrorString(e));
+    return B200_ATTN_ERR_LAUNCH;
+  }
+  return B200_ATTN_OK;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace b200ln
+
+using namespace b200ln;
+
+extern "C" int32_t b200_layernorm_check(const b200_layernorm_params* p) {
+  if (!p || !p->x || !p->y) return B200_ATTN_ERR_INVALID_ARGUMENT;
+  if (p->rows < 1 || p->cols < 1 || p->rows > (1ll << 40)) return B200_ATTN_ERR_INVALID_ARGUMENT;
+  if (!(p->eps > 0.f) || !std::isfinite(p->eps)) return B200_ATTN_ERR_INVALID_ARGUMENT;
+  if (p->dtype != B200_ATTN_DTYPE_BF16 && p->dtype != B200_ATTN_DTYPE_FP16)
+    return B200_ATTN_ERR_UNSUPPORTED;
+  if (p->cols > kMaxCols) return B200_ATTN_ERR_UNSUPPORTED;
+  if (p->rows > 1 && (p->x_row_stride < p->cols || p->y_row_stride < p->cols))
+    return B200_ATTN_ERR_INVALID_ARGUMENT;
+  if (p->cols % 8 != 0) return B200_ATTN_ERR_ALIGNMENT;
+  if (!aligned16(p->x) || !aligned16(p->y)) return B200_ATTN_ERR_ALIGNMENT;
+  if ((p->weight && !aligned16(p->weight)) || (p->bias && !aligned16(p->bias)))
+    return B200_ATTN_ERR_ALIGNMENT;
+  if (p->rows > 1 && (p->x_row_stride % 8 != 0 || p->y_row_stride % 8 != 0))
+    return B200_ATTN_ERR_ALIGNMENT;
+  return B200_ATTN_OK;
+}
+
+extern "C" int32_t b200_layernorm_fwd(const b200_layernorm_params* p, void* stream) {
+  const int32_t rc = b200_layernorm_check(p);
+  if (rc != B200_ATTN_OK) return rc;
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, p->x) != cudaSuccess || attr.device < 0 ||
+      (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)) {
+    cudaGetLastError();
+    set_error("x is not a device pointer");
+    return B200_ATTN_ERR_DEVICE;
+  }
+  DeviceGuard guard;
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != attr.device) {
+    if (cudaSetDevice(attr.device) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("cudaSetDevice failed");
+      return B200_ATTN_ERR_DEVICE;
+    }
+    guard.prev = cur;
+  }
+  LnArgs a;
+  a.x = static_cast<const uint16_t*>(p->x);
+  a.w = static_cast<const uint16_t*>(p->weight);
+  a.b = static_cast<const uint16_t*>(p->bias);
+  a.y = static_cast<uint16_t*>(p->y);
+  a.rows = p->rows;
+  a.cols = static_cast<int32_t>(p->cols);
+  a.ldx = p->x_row_stride;
+  a.ldy = p->y_row_stride;
+  a.eps = p->eps;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return p->dtype == B200_ATTN_DTYPE_BF16 ? launch<true>(a, s) : launch<false>(a, s);
+}
