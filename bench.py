@@ -466,8 +466,8 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
                    "parallelism": f"data-parallel batch split x{world}, no data-path collective",
                    "launch": "CUDA graph of the whole forward" if graph is not None else "eager",
                    "epilogues": ("fused linear kernel: out_proj + residual, ffn_in + GELU "
-                                 "(QKV and ffn_out on cuBLAS)") if fused else
-                                "cuBLAS linear layers + separate GELU / add passes",
+                                 "(QKV and ffn_out on cuBLAS); LayerNorm kernel") if fused else
+                                "cuBLAS linear layers + separate GELU / add passes; torch LayerNorm",
                    "l2": f"{n_sets} token sets; each forward streams ~0.4 GB of weights and activations (> L2)",
                    "flop_per_step_job": flop_job},
         "attention": {"tflops": attn_tflops, "ms_per_layer": attn_ms,
@@ -480,8 +480,9 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
         "e2e": {"value": flop_rank / (e2e_ms * 1e-3) / 1e12 * world, "unit": "TFLOP/s (decoder forward)",
                 "h2d_bytes_per_step": htok.numel() * htok.element_size(),
                 "d2h_bytes_per_step": hout.numel() * hout.element_size(), "ms_per_step": e2e_ms},
-        # per layer: the attention kernel, plus out_proj and ffn_in on the fused linear kernel
-        "gpu_launches": args.steps * cfg["layers"] * (3 if fused else 1),
+        # per layer: the attention kernel, plus (fused) out_proj and ffn_in on the
+        # fused linear kernel and norm1/norm2 on the LayerNorm kernel; and the final norm
+        "gpu_launches": args.steps * (cfg["layers"] * 5 + 1 if fused else cfg["layers"]),
         "clocks": sampler.summary(),
         "validation": {"finite": finite, "device_errors": errors},
     }

@@ -89,10 +89,11 @@ typedef struct b200_attn_fwd_params {
 /* ABI version (B200_ATTN_ABI_VERSION). */
 B200_ATTN_API int32_t b200_attn_abi_version(void);
 
-/* Host-only envelope query: 1 when the kernel computes (dtype, head_dim)
- * natively for the given causal/mask flags (head_dim 64 or 128), else 0.  Makes
- * no CUDA call.  (The Python operator and planner also accept other multiples
- * of 8 up to 128 by zero-padding them to 64 or 128.)
+/* Host-only envelope query: 1 when the kernel computes (dtype, head_dim) for
+ * the given causal/mask flags (head_dim any multiple of 8 up to 128), else 0.
+ * Makes no CUDA call.  Head dims below 64 (above 64) run the 64-wide (128-wide)
+ * kernel instance with the missing columns read as zeros by TMA; the result is
+ * that of the true head dim.
  * Replaces the support test of triton_fused_attention
  * (model/triton_fused_attention.py:1906-1921) and the planner's envelope
  * (model/attention_dispatch.py:399-459). */

@@ -78,8 +78,8 @@ class FallbackReason(_TextEnum):
 # Envelope of the sm_100a kernel; the C ABI's b200_attn_query answers the same
 # question and a CPU test keeps the two in agreement.
 SM100_DTYPES = ("bfloat16", "float16")
-# 64 and 128 run natively; other multiples of 8 up to 128 are zero-padded to
-# the next of those by the operator.
+# Every multiple of 8 up to 128: narrower heads run the 64- or 128-wide kernel
+# instance with the missing columns read as zeros by TMA.
 SM100_HEAD_DIMS = tuple(range(8, 129, 8))
 SM100_CAPABILITY_MAJOR = 10
 

@@ -19,6 +19,7 @@ planner's decision (``attention_dispatch``), made visibly, not the operator's.
 from __future__ import annotations
 
 import ctypes
+import struct
 import threading
 from typing import Optional
 
@@ -27,11 +28,12 @@ import torch
 from . import _native
 
 SUPPORTED_DTYPES = {torch.bfloat16: _native.DTYPE_BF16, torch.float16: _native.DTYPE_FP16}
-NATIVE_HEAD_DIMS = (64, 128)  # what the kernel computes directly
-# Other head dims (multiples of 8 up to 128) are zero-padded to the next native
-# size: zero columns add nothing to Q K^T, and V's zero columns give output
-# columns that are dropped; the softmax scale stays that of the true head dim.
+# Every multiple of 8 up to 128.  The kernel's 64- and 128-wide instances read
+# the missing columns of narrower heads as zeros through TMA (zero columns add
+# nothing to Q K^T and P V) and its output store clips them; the softmax scale
+# stays that of the true head dim.  No padded copies are made.
 SUPPORTED_HEAD_DIMS = tuple(range(8, 129, 8))
+NATIVE_HEAD_DIMS = SUPPORTED_HEAD_DIMS
 BLOCK_M = 128  # query rows per tile (two tiles per CTA)
 BLOCK_N = 128  # keys per K/V tile
 
@@ -106,24 +108,6 @@ def _capability_major(device: torch.device) -> int:
     return major
 
 
-def _padded_head_dim(q, k, v, valid_token_mask, causal, scale, output_bshd,
-                     zero_masked_queries, out):
-    """Head dims other than 64/128: run the kernel on copies zero-padded to the
-    next native head dim and keep the first ``head_dim`` output columns."""
-    head_dim = q.shape[-1]
-    padded = 64 if head_dim <= 64 else 128
-    pad = lambda t: torch.nn.functional.pad(t, (0, padded - head_dim))
-    res = b200_fused_attention(pad(q), pad(k), pad(v), valid_token_mask, causal, scale,
-                               output_bshd, zero_masked_queries=zero_masked_queries)
-    res = res[..., :head_dim]
-    if out is not None:
-        if tuple(out.shape) != tuple(res.shape):
-            raise ValueError(f"out must have shape {tuple(res.shape)}")
-        out.copy_(res)
-        return out
-    return res.contiguous()
-
-
 def device_error_word(device: torch.device) -> torch.Tensor:
     """Per-device int32 the kernel ORs error bits into (allocated once)."""
     index = device.index if device.index is not None else torch.cuda.current_device()
@@ -153,6 +137,14 @@ def _strides(t: torch.Tensor) -> tuple[int, int, int]:
     return (t.stride(0), t.stride(1), t.stride(2))
 
 
+# b200_attn_fwd_params packed in one call (layout checked against the ctypes
+# mirror at import): q k v o, B H S D, four stride triples, mask and its two
+# strides, scale, dtype, causal, zero_masked_queries, error word.
+_FWD_LAYOUT = struct.Struct("=4Q4q12qQ2qfiiiQ")
+assert _FWD_LAYOUT.size == ctypes.sizeof(_native.FwdParams)
+assert _native.FwdParams.error_word.offset == _FWD_LAYOUT.size - 8
+
+
 def make_params(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -165,22 +157,17 @@ def make_params(
     error_word: Optional[torch.Tensor],
 ) -> _native.FwdParams:
     """Fill the C parameter struct from tensors (``out_bhsd`` is a [B,H,S,D] view)."""
-    batch, heads, seq_len, head_dim = q.shape
     p = _native.FwdParams()
-    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), out_bhsd.data_ptr()
-    p.batch, p.heads, p.seq_len, p.head_dim = batch, heads, seq_len, head_dim
-    p.q_stride[:] = _strides(q)
-    p.k_stride[:] = _strides(k)
-    p.v_stride[:] = _strides(v)
-    p.o_stride[:] = _strides(out_bhsd)
     if valid_token_mask is not None:
-        p.key_mask = valid_token_mask.data_ptr()
-        p.mask_stride[:] = (valid_token_mask.stride(0), valid_token_mask.stride(1))
-    p.scale = float(scale)
-    p.dtype = SUPPORTED_DTYPES[q.dtype]
-    p.causal = 1 if causal else 0
-    p.zero_masked_queries = 1 if zero_masked_queries else 0
-    p.error_word = error_word.data_ptr() if error_word is not None else None
+        mask, ms0, ms1 = (valid_token_mask.data_ptr(), valid_token_mask.stride(0),
+                          valid_token_mask.stride(1))
+    else:
+        mask = ms0 = ms1 = 0
+    _FWD_LAYOUT.pack_into(
+        p, 0, q.data_ptr(), k.data_ptr(), v.data_ptr(), out_bhsd.data_ptr(), *q.shape,
+        *q.stride()[:3], *k.stride()[:3], *v.stride()[:3], *out_bhsd.stride()[:3],
+        mask, ms0, ms1, float(scale), SUPPORTED_DTYPES[q.dtype], 1 if causal else 0,
+        1 if zero_masked_queries else 0, error_word.data_ptr() if error_word is not None else 0)
     return p
 
 
@@ -228,10 +215,6 @@ def b200_fused_attention(
         raise ValueError(f"unsupported sm_100a attention invocation: {reason}")
     if zero_masked_queries and valid_token_mask is None:
         raise ValueError("zero_masked_queries requires valid_token_mask")
-    if head_dim not in NATIVE_HEAD_DIMS:
-        return _padded_head_dim(q, k, v, valid_token_mask, causal, scale, output_bshd,
-                                zero_masked_queries, out)
-
     if output_bshd:
         shape = (batch, seq_len, heads, head_dim)
         if out is None:

@@ -12,6 +12,7 @@ Inference only; anything outside the envelope raises ``ValueError``.
 from __future__ import annotations
 
 import ctypes
+import struct
 from typing import Optional
 
 import torch
@@ -20,6 +21,11 @@ from . import _native
 from .fused_attention import SUPPORTED_DTYPES
 
 MAX_COLS = 4096
+
+# b200_layernorm_params packed in one call (layout checked against the ctypes
+# mirror at import): x weight bias y, rows cols and the two row strides, eps, dtype.
+_LN_LAYOUT = struct.Struct("=4Q4qfi")
+assert _LN_LAYOUT.size == ctypes.sizeof(_native.LayerNormParams)
 
 
 def layer_norm_supported(x: torch.Tensor, weight: Optional[torch.Tensor]) -> bool:
@@ -75,13 +81,9 @@ def b200_layer_norm(x: torch.Tensor, weight: Optional[torch.Tensor] = None,
     x2 = _rows(x, cols)
     y2 = y.view(-1, cols)
     p = _native.LayerNormParams()
-    p.x, p.y = x2.data_ptr(), y2.data_ptr()
-    p.weight = w.data_ptr() if w is not None else None
-    p.bias = b.data_ptr() if b is not None else None
-    p.rows, p.cols = x2.shape[0], cols
-    p.x_row_stride, p.y_row_stride = x2.stride(0), y2.stride(0)
-    p.eps = float(eps)
-    p.dtype = SUPPORTED_DTYPES[x.dtype]
+    _LN_LAYOUT.pack_into(p, 0, x2.data_ptr(), w.data_ptr() if w is not None else 0,
+                         b.data_ptr() if b is not None else 0, y2.data_ptr(), x2.shape[0], cols,
+                         x2.stride(0), y2.stride(0), float(eps), SUPPORTED_DTYPES[x.dtype])
     lib = _native.load_library()
     rc = lib.b200_layernorm_fwd(ctypes.byref(p),
                                 ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream))

@@ -23,12 +23,20 @@ no fallback to another implementation.
 from __future__ import annotations
 
 import ctypes
+import struct
 from typing import Optional
 
 import torch
 
 from . import _native
 from .fused_attention import SUPPORTED_DTYPES, device_error_word
+
+# b200_linear_params packed in one call (layout checked against the ctypes
+# mirror at import): six pointers, m n k, four row strides, dtype, activation,
+# masked_rows, reserved, error word.
+_LINEAR_LAYOUT = struct.Struct("=6Q7q4iQ")
+assert _LINEAR_LAYOUT.size == ctypes.sizeof(_native.LinearParams)
+assert _native.LinearParams.error_word.offset == _LINEAR_LAYOUT.size - 8
 
 _MASKED_ROWS = {"zero": _native.LINEAR_MASKED_ZERO,
                 "residual": _native.LINEAR_MASKED_KEEP_RESIDUAL}
@@ -119,19 +127,13 @@ def b200_linear(
     y2 = y.view(-1, n)
 
     p = _native.LinearParams()
-    p.x, p.w, p.y = x2.data_ptr(), w2.data_ptr(), y2.data_ptr()
-    p.bias = b1.data_ptr() if b1 is not None else None
-    p.residual = r2.data_ptr() if r2 is not None else None
-    p.row_mask = m1.data_ptr() if m1 is not None else None
-    p.m, p.n, p.k = x2.shape[0], n, k
-    p.x_row_stride = x2.stride(0)
-    p.w_row_stride = w2.stride(0)
-    p.residual_row_stride = r2.stride(0) if r2 is not None else 0
-    p.y_row_stride = y2.stride(0)
-    p.dtype = SUPPORTED_DTYPES[x.dtype]
-    p.activation = _ACTIVATIONS[activation]
-    p.masked_rows = _MASKED_ROWS[masked_rows]
-    p.error_word = device_error_word(x.device).data_ptr()
+    _LINEAR_LAYOUT.pack_into(
+        p, 0, x2.data_ptr(), w2.data_ptr(), b1.data_ptr() if b1 is not None else 0,
+        r2.data_ptr() if r2 is not None else 0, m1.data_ptr() if m1 is not None else 0,
+        y2.data_ptr(), x2.shape[0], n, k, x2.stride(0), w2.stride(0),
+        r2.stride(0) if r2 is not None else 0, y2.stride(0), SUPPORTED_DTYPES[x.dtype],
+        _ACTIVATIONS[activation], _MASKED_ROWS[masked_rows], 0,
+        device_error_word(x.device).data_ptr())
 
     lib = _native.load_library()
     stream = torch.cuda.current_stream(x.device).cuda_stream

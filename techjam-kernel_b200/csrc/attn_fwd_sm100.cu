@@ -106,6 +106,7 @@ struct KernelArgs {
   int32_t heads;
   int32_t batch;
   int32_t num_q_blocks;  // ceil(S / 256)
+  int32_t head_dim;      // the tensors' head dim (<= the instance's D)
   int32_t group_heads;   // (batch, head) pairs per L2 group of CTAs
   float scale;           // softmax scale
   float scale_log2;      // scale * log2(e)
@@ -473,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             reinterpret_cast<uint16_t*>(args.o) + static_cast<int64_t>(b) * args.o_sb +
             static_cast<int64_t>(h) * args.o_sh + static_cast<int64_t>(row) * args.o_ss);
 #pragma unroll
-        for (int c = 0; c < D / 8; ++c) dst[c] = make_uint4(0u, 0u, 0u, 0u);
+        for (int c = 0; c < args.head_dim / 8; ++c) dst[c] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
     return;
@@ -988,7 +989,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-bool supported_head_dim(int64_t d) { return d == 64 || d == 128; }
+// Any multiple of 8 up to 128.  The instance with D = 64 serves head dims up to
+// 64, D = 128 the rest: the tensor maps give the true head dim as the inner
+// extent, so the 64-column TMA boxes read zeros past it (Q K^T and P V are
+// unchanged by zero columns) and the output store clips the columns past it.
+bool supported_head_dim(int64_t d) { return d >= 8 && d <= 128 && d % 8 == 0; }
+bool wide_head(int64_t d) { return d > 64; }
 
 // Alignment rules of the 4-D TMA view {D, S, H, B}: 16-byte base, 16-byte
 // multiples for every stride whose dimension has extent > 1.
@@ -1182,7 +1188,7 @@ int32_t prepare(const b200_attn_fwd_params* p, CUtensorMap maps[4], KernelArgs& 
     return B200_ATTN_ERR_DEVICE;
   }
 
-  const uint32_t kv_rows = p->head_dim == 128 ? Cfg128::BN : Cfg64::BN;
+  const uint32_t kv_rows = wide_head(p->head_dim) ? Cfg128::BN : Cfg64::BN;
   if ((rc = encode_map(&maps[0], p->q, p->q_stride, p, kBlockM)) != B200_ATTN_OK ||
       (rc = encode_map(&maps[1], p->k, p->k_stride, p, kv_rows)) != B200_ATTN_OK ||
       (rc = encode_map(&maps[2], p->v, p->v_stride, p, kv_rows)) != B200_ATTN_OK ||
@@ -1190,6 +1196,7 @@ int32_t prepare(const b200_attn_fwd_params* p, CUtensorMap maps[4], KernelArgs& 
     return rc;
 
   a.seq_len = static_cast<int32_t>(p->seq_len);
+  a.head_dim = static_cast<int32_t>(p->head_dim);
   a.heads = static_cast<int32_t>(p->heads);
   a.batch = static_cast<int32_t>(p->batch);
   a.num_q_blocks = static_cast<int32_t>((p->seq_len + kRowsPerCta - 1) / kRowsPerCta);
@@ -1232,7 +1239,7 @@ extern "C" int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream) {
   const int32_t rc = prepare(p, maps, a, dev, guard);
   if (rc != B200_ATTN_OK) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (p->head_dim == 128) return dispatch_flags<Cfg128>(maps, a, p, dev, s);
+  if (wide_head(p->head_dim)) return dispatch_flags<Cfg128>(maps, a, p, dev, s);
   return dispatch_flags<Cfg64>(maps, a, p, dev, s);
 }
 

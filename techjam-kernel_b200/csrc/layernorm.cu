@@ -3,7 +3,8 @@
 // torch_transformer_benchmark.py:141-142, 170):
 //   y = (x - mean) * rsqrt(var + eps) * weight + bias
 // mean and biased variance in fp32 (two passes over the row held in
-// registers), the affine step in fp32, one rounding to the element type.
+// registers, widened once), the affine step ((x - mean) * rstd * weight + bias)
+// in fp32, one rounding to the element type.
 //
 // HBM-bound: one warp per row, 16-byte loads and stores (a warp reads and
 // writes whole contiguous 512-byte segments), the row kept in registers
@@ -69,7 +70,34 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// VPL: 16-byte vectors per lane (8 elements each), cols <= 256 * VPL.
+// Packed fp32 pairs (sm_100 .f32x2): each lane rounds like the scalar op.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// VPL: 16-byte vectors per lane (8 elements each), cols <= 256 * VPL.  The
+// row is widened to fp32 once and kept in registers (4 * VPL pairs per lane).
 template <int VPL, bool BF16>
 __global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
   const int warp = threadIdx.x >> 5;
@@ -77,36 +105,36 @@ __global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + warp;
   if (row >= a.rows) return;
   const uint16_t* xr = a.x + row * a.ldx;
-  uint4 v[VPL];
-  float s = 0.f;
+  float2 f[VPL][4];
+  float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int col = (i * 32 + lane) * 8;
-    v[i] = col < a.cols ? __ldg(reinterpret_cast<const uint4*>(xr + col)) : make_uint4(0u, 0u, 0u, 0u);
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[i]);
+    const uint4 v =
+        col < a.cols ? __ldg(reinterpret_cast<const uint4*>(xr + col)) : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float2 f = unpack2<BF16>(w[j]);
-      s += f.x + f.y;
+      f[i][j] = unpack2<BF16>(w[j]);
+      s2 = add2(s2, f[i][j]);
     }
   }
   const float inv_n = 1.f / static_cast<float>(a.cols);
-  const float mean = warp_sum(s) * inv_n;
-  float q = 0.f;
+  const float mean = warp_sum(s2.x + s2.y) * inv_n;
+  const float2 neg_mean = make_float2(-mean, -mean);
+  float2 q2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int col = (i * 32 + lane) * 8;
     if (col >= a.cols) continue;  // padding lanes hold zeros, not x - mean
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[i]);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float2 f = unpack2<BF16>(w[j]);
-      const float d0 = f.x - mean, d1 = f.y - mean;
-      q = fmaf(d0, d0, q);
-      q = fmaf(d1, d1, q);
+      const float2 d = add2(f[i][j], neg_mean);
+      q2 = fma2(d, d, q2);
     }
   }
-  const float rstd = rsqrtf(warp_sum(q) * inv_n + a.eps);
+  const float rstd = rsqrtf(warp_sum(q2.x + q2.y) * inv_n + a.eps);
+  const float2 r2 = make_float2(rstd, rstd);
   uint16_t* yr = a.y + row * a.ldy;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
@@ -114,16 +142,16 @@ __global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
     if (col >= a.cols) continue;
     const uint4 g4 = a.w ? __ldg(reinterpret_cast<const uint4*>(a.w + col)) : make_uint4(0u, 0u, 0u, 0u);
     const uint4 b4 = a.b ? __ldg(reinterpret_cast<const uint4*>(a.b + col)) : make_uint4(0u, 0u, 0u, 0u);
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[i]);
     const uint32_t* gw = reinterpret_cast<const uint32_t*>(&g4);
     const uint32_t* bw = reinterpret_cast<const uint32_t*>(&b4);
     uint32_t o[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float2 f = unpack2<BF16>(w[j]);
+      const float2 n = mul2(add2(f[i][j], neg_mean), r2);  // (x - mean) * rstd
       const float2 g = a.w ? unpack2<BF16>(gw[j]) : make_float2(1.f, 1.f);
       const float2 bb = a.b ? unpack2<BF16>(bw[j]) : make_float2(0.f, 0.f);
-      o[j] = pack2<BF16>(fmaf((f.x - mean) * rstd, g.x, bb.x), fmaf((f.y - mean) * rstd, g.y, bb.y));
+      const float2 y = fma2(n, g, bb);
+      o[j] = pack2<BF16>(y.x, y.y);
     }
     *reinterpret_cast<uint4*>(yr + col) = make_uint4(o[0], o[1], o[2], o[3]);
   }

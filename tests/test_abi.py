@@ -67,14 +67,12 @@ def test_abi_version(lib):
 
 
 def test_query_agrees_with_planner_envelope(lib):
-    """The C ABI reports the kernel's native head dims; the planner's envelope
-    adds the head dims the operator zero-pads to them (multiples of 8 up to 128)."""
+    """The C ABI and the planner agree on the head dims the kernel computes:
+    every multiple of 8 up to 128."""
     for dtype in (_native.DTYPE_BF16, _native.DTYPE_FP16, 7):
-        for d in (16, 32, 64, 96, 128, 256):
-            native = 1 if dtype in (0, 1) and d in (64, 128) else 0
-            assert lib.b200_attn_query(dtype, d, 1, 0) == native
-            if native:
-                assert d in SM100_HEAD_DIMS
+        for d in (0, 4, 8, 12, 16, 32, 60, 64, 96, 120, 128, 136, 256):
+            supported = 1 if dtype in (0, 1) and d in SM100_HEAD_DIMS else 0
+            assert lib.b200_attn_query(dtype, d, 1, 0) == supported
     assert set(SM100_HEAD_DIMS) == set(range(8, 129, 8))
 
 
@@ -115,8 +113,8 @@ def test_check_accepts_valid_params(lib):
     (dict(scale=-1.0), _native.ERR_INVALID_ARGUMENT),
     (dict(scale=float("inf")), _native.ERR_INVALID_ARGUMENT),
     (dict(dtype=5), _native.ERR_UNSUPPORTED),
-    (dict(head_dim=96), _native.ERR_UNSUPPORTED),
-    (dict(head_dim=32), _native.ERR_UNSUPPORTED),
+    (dict(head_dim=136), _native.ERR_UNSUPPORTED),
+    (dict(head_dim=100), _native.ERR_UNSUPPORTED),
     (dict(q=0x10008), _native.ERR_ALIGNMENT),
     (dict(zero_masked_queries=1), _native.ERR_INVALID_ARGUMENT),
 ])
@@ -137,3 +135,15 @@ def test_error_strings(lib):
     for code in range(7):
         assert lib.b200_attn_error_string(code)
     assert b"unknown" in lib.b200_attn_error_string(99)
+
+
+def test_packed_layout_fills_every_field_in_order():
+    from b200_attention.fused_attention import _FWD_LAYOUT
+    p = _native.FwdParams()
+    ints = list(range(1, 26))  # 4 pointers, 4 sizes, 12 strides, mask pointer, 2 mask strides
+    _FWD_LAYOUT.pack_into(p, 0, *ints[:23], 0.25, 26, 27, 28, 29)
+    assert [p.q, p.k, p.v, p.o] == ints[:4]
+    assert [p.batch, p.heads, p.seq_len, p.head_dim] == ints[4:8]
+    assert list(p.q_stride) + list(p.k_stride) + list(p.v_stride) + list(p.o_stride) == ints[8:20]
+    assert p.key_mask == 21 and list(p.mask_stride) == [22, 23]
+    assert (p.scale, p.dtype, p.causal, p.zero_masked_queries, p.error_word) == (0.25, 26, 27, 28, 29)

@@ -31,6 +31,10 @@ CASES = [
     (3, 2, 700, 64, False, [700, 333, 1], True),
     (1, 2, 1000, 128, True, None, False),
     (2, 1, 1536, 128, False, [1536, 700], True),
+    # narrow heads: the 64- / 128-wide instance reads zeros past the head dim
+    (2, 2, 300, 32, True, [300, 123], True),
+    (1, 3, 129, 8, False, None, False),
+    (2, 1, 257, 96, True, None, False),
 ]
 
 

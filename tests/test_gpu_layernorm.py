@@ -45,7 +45,7 @@ def test_shapes(shape):
 
 @pytest.mark.parametrize("kw", [dict(affine=False), dict(dtype=torch.float16),
                                 dict(scale=30.0, shift=5.0), dict(shift=100.0, scale=0.5),
-                                dict(eps=1e-2)],
+                                dict(shift=1000.0, scale=0.0), dict(eps=1e-2)],
                          ids=lambda kw: "-".join(f"{k}={v}" for k, v in kw.items()))
 def test_variants(kw):
     _check((257, 1024), **kw)

@@ -114,7 +114,7 @@ def test_operator_replays_in_a_cuda_graph():
 def test_published_matrix_shapes_with_small_heads(batch, d_model, heads, seq_len):
     """The reference's announced benchmark cases mostly use d_model 128 with 4
     heads (D = 32) or 16 heads (D = 8); on a B200 they plan the sm_100a kernel
-    through zero padding and must match the baseline order."""
+    (narrow heads read as zero-extended tiles) and must match the baseline order."""
     dev = torch.device("cuda", 0)
     torch.manual_seed(3)
     mod = B200FusedSelfAttention(d_model, heads).to(dev, torch.bfloat16).eval()

@@ -93,3 +93,11 @@ def test_python_argument_errors():
         b200_layer_norm(x, eps=0.0)
     with pytest.raises(ValueError, match="inference-only"):
         b200_layer_norm(x, torch.ones(64, dtype=torch.bfloat16, requires_grad=True))
+
+
+def test_packed_layout_fills_every_field_in_order():
+    from b200_attention.layernorm import _LN_LAYOUT
+    p = _native.LayerNormParams()
+    values = [1, 2, 3, 4, 5, 6, 7, 8, 0.5, 9]
+    _LN_LAYOUT.pack_into(p, 0, *values)
+    assert [getattr(p, f) for f, _ in _native.LayerNormParams._fields_] == values

@@ -114,3 +114,12 @@ def test_tile_width(lib):
     assert lib.b200_linear_tile_n(ctypes.byref(_params()), 148) == 256
     assert lib.b200_linear_tile_n(ctypes.byref(_params(n=128, y_row_stride=128)), 148) == 128
     assert lib.b200_linear_tile_n(ctypes.byref(_params(m=0)), 148) == 0
+
+
+def test_packed_layout_fills_every_field_in_order():
+    from b200_attention.linear import _LINEAR_LAYOUT
+    p = _native.LinearParams()
+    values = list(range(1, 19))
+    _LINEAR_LAYOUT.pack_into(p, 0, *values)
+    got = [getattr(p, f) for f, _ in _native.LinearParams._fields_]
+    assert got == values

@@ -80,7 +80,7 @@ def test_b200_gates():
     assert mism.reason == FallbackReason.SHAPE_MISMATCH
     cpu = select_attention_stack_plan(spec, _rt(device="cpu", cap=None)).layers[0]
     assert cpu.reason == FallbackReason.UNSUPPORTED_DEVICE
-    d32 = AttentionModelSpec(8, 2048, 512, 16, 512, 1, True)  # zero-padded to 64 by the operator
+    d32 = AttentionModelSpec(8, 2048, 512, 16, 512, 1, True)  # D = 32: the 64-wide instance
     assert select_attention_stack_plan(d32, _rt(d=512)).layers[0].mode == AttentionMode.SM100_FUSED
     d12 = AttentionModelSpec(8, 2048, 192, 16, 512, 1, True)  # 12: not a multiple of 8
     assert select_attention_stack_plan(d12, _rt(d=192)).layers[0].reason == FallbackReason.UNVALIDATED_SHAPE
