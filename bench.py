@@ -424,20 +424,41 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
         attn_flop = 4.0 * B * H * S * S * D / 2
         errors = read_device_errors(dev)
 
-        # end to end: token ids from pinned host memory, output back to the host
-        htok = tokens[0].cpu().pin_memory()
-        hout = torch.empty((B, S, cfg["d_model"]), dtype=torch.bfloat16).pin_memory()
-        for _ in range(2):
-            hout.copy_(forward(htok.to(dev, non_blocking=True)), non_blocking=True)
+        # end to end: token ids from pinned host memory, output back to the host,
+        # every step.  Steps are pipelined the way a server streams batches: the
+        # forward of step i+1 runs while step i's output is copied to the host on
+        # a copy stream (two device staging buffers, two pinned host buffers).
+        htoks = [t.cpu().pin_memory() for t in tokens]
+        houts = [torch.empty((B, S, cfg["d_model"]), dtype=torch.bfloat16).pin_memory()
+                 for _ in range(2)]
+        stage = [torch.empty((B, S, cfg["d_model"]), dtype=torch.bfloat16, device=dev)
+                 for _ in range(2)]
+        d2h_stream = torch.cuda.Stream(dev)
+        copied = [torch.cuda.Event() for _ in range(2)]
+
+        def e2e_step(i):
+            j = i % 2
+            stream.wait_event(copied[j])  # step i-2's download has left stage[j]
+            out_i = forward(htoks[i % n_sets].to(dev, non_blocking=True))
+            stage[j].copy_(out_i, non_blocking=True)
+            d2h_stream.wait_stream(stream)
+            with torch.cuda.stream(d2h_stream):
+                houts[j].copy_(stage[j], non_blocking=True)
+                copied[j].record(d2h_stream)
+
+        for i in range(2):
+            e2e_step(i)
         torch.cuda.synchronize(dev)
         barrier()
         e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
         e0.record(stream)
-        for _ in range(e2e_steps):
-            hout.copy_(forward(htok.to(dev, non_blocking=True)), non_blocking=True)
+        for i in range(e2e_steps):
+            e2e_step(i)
+        stream.wait_stream(d2h_stream)
         e1.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
+        hout = houts[(e2e_steps - 1) % 2]
         e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
 
     cpu = None
@@ -478,8 +499,9 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
                      "peak_source": f"{peak_src} bf16_tflops (burst, kernel timed alone)"},
         "cpu_baseline": cpu,
         "e2e": {"value": flop_rank / (e2e_ms * 1e-3) / 1e12 * world, "unit": "TFLOP/s (decoder forward)",
-                "h2d_bytes_per_step": htok.numel() * htok.element_size(),
-                "d2h_bytes_per_step": hout.numel() * hout.element_size(), "ms_per_step": e2e_ms},
+                "h2d_bytes_per_step": htoks[0].numel() * htoks[0].element_size(),
+                "d2h_bytes_per_step": hout.numel() * hout.element_size(), "ms_per_step": e2e_ms,
+                "pipelining": "step i+1's forward overlaps step i's download (copy stream)"},
         # per layer: the attention kernel, plus (fused) out_proj and ffn_in on the
         # fused linear kernel and norm1/norm2 on the LayerNorm kernel; and the final norm
         "gpu_launches": args.steps * (cfg["layers"] * 5 + 1 if fused else cfg["layers"]),
