@@ -459,6 +459,9 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
         torch.cuda.synchronize(dev)
         barrier()
         hout = houts[(e2e_steps - 1) % 2]
+        # the last download equals a fresh forward of the same tokens (every
+        # kernel on the path is deterministic)
+        e2e_exact = bool(torch.equal(hout, forward(tokens[(e2e_steps - 1) % n_sets]).cpu()))
         e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
 
     cpu = None
@@ -506,7 +509,7 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
         # fused linear kernel and norm1/norm2 on the LayerNorm kernel; and the final norm
         "gpu_launches": args.steps * (cfg["layers"] * 5 + 1 if fused else cfg["layers"]),
         "clocks": sampler.summary(),
-        "validation": {"finite": finite, "device_errors": errors},
+        "validation": {"finite": finite, "device_errors": errors, "e2e_bit_exact": e2e_exact},
     }
     print(json.dumps(line), flush=True)
     return 0
