@@ -189,7 +189,9 @@ using namespace b200ln;
 
 extern "C" int32_t b200_layernorm_check(const b200_layernorm_params* p) {
   if (!p || !p->x || !p->y) return B200_ATTN_ERR_INVALID_ARGUMENT;
-  if (p->rows < 1 || p->cols < 1 || p->rows > (1ll << 40)) return B200_ATTN_ERR_INVALID_ARGUMENT;
+  // one block per kRowsPerBlock rows, at most 2^31 - 1 blocks
+  if (p->rows < 1 || p->cols < 1 || p->rows > static_cast<int64_t>(kRowsPerBlock) * 0x7fffffffll)
+    return B200_ATTN_ERR_INVALID_ARGUMENT;
   if (!(p->eps > 0.f) || !std::isfinite(p->eps)) return B200_ATTN_ERR_INVALID_ARGUMENT;
   if (p->dtype != B200_ATTN_DTYPE_BF16 && p->dtype != B200_ATTN_DTYPE_FP16)
     return B200_ATTN_ERR_UNSUPPORTED;
