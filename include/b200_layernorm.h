@@ -12,6 +12,12 @@
  * x and y are row-major [rows, cols] with a contiguous last dimension (row
  * strides in ELEMENTS); weight and bias are [cols] or NULL (1 and 0).  Element
  * types are B200_ATTN_DTYPE_* (b200_attn.h); return codes are B200_ATTN_*.
+ *
+ * With an addend the call first forms the block's residual sum
+ *   s = x + addend            (an fp32 add rounded once, like a 16-bit tensor add)
+ * writes it to `sum` (when not NULL) and normalises s instead of x: the
+ * residual add that ends one reference block (torch_transformer_benchmark.py:142)
+ * fused with the LayerNorm that starts the next (:141) or the final norm (:170).
  */
 #ifndef B200_LAYERNORM_H_
 #define B200_LAYERNORM_H_
@@ -33,6 +39,10 @@ typedef struct b200_layernorm_params {
   int64_t y_row_stride;
   float eps;              /* > 0 */
   int32_t dtype;          /* B200_ATTN_DTYPE_* */
+  const void* addend;     /* [rows, cols] or NULL: normalise x + addend */
+  void* sum;              /* [rows, cols] or NULL: receives x + addend (may be x itself) */
+  int64_t addend_row_stride;
+  int64_t sum_row_stride;
 } b200_layernorm_params;
 
 /* Host-only validation (sizes, dtype, eps, 16-byte alignment of bases and row

@@ -123,6 +123,10 @@ class LayerNormParams(ctypes.Structure):
         ("y_row_stride", ctypes.c_int64),
         ("eps", ctypes.c_float),
         ("dtype", ctypes.c_int32),
+        ("addend", ctypes.c_void_p),
+        ("sum", ctypes.c_void_p),
+        ("addend_row_stride", ctypes.c_int64),
+        ("sum_row_stride", ctypes.c_int64),
     ]
 
 

@@ -5,7 +5,8 @@
 variance and the affine step in fp32, one rounding to the element type) for
 bf16/fp16 inputs whose last dimension is a multiple of 8 up to 4096.  It
 replaces the reference block's norm1/norm2 and the model's final norm
-(torch_transformer_benchmark.py:141-142, 170) in the decoder's fused path.
+(torch_transformer_benchmark.py:141-142, 170) in the decoder's fused path;
+``b200_add_layer_norm`` also forms the residual sum that precedes the norm.
 Inference only; anything outside the envelope raises ``ValueError``.
 """
 
@@ -23,8 +24,9 @@ from .fused_attention import SUPPORTED_DTYPES
 MAX_COLS = 4096
 
 # b200_layernorm_params packed in one call (layout checked against the ctypes
-# mirror at import): x weight bias y, rows cols and the two row strides, eps, dtype.
-_LN_LAYOUT = struct.Struct("=4Q4qfi")
+# mirror at import): x weight bias y, rows cols and the two row strides, eps,
+# dtype, addend and sum pointers and their row strides.
+_LN_LAYOUT = struct.Struct("=4Q4qfi2Q2q")
 assert _LN_LAYOUT.size == ctypes.sizeof(_native.LayerNormParams)
 
 
@@ -59,6 +61,27 @@ def _vector(t: Optional[torch.Tensor], cols: int, name: str, x: torch.Tensor):
 def b200_layer_norm(x: torch.Tensor, weight: Optional[torch.Tensor] = None,
                     bias: Optional[torch.Tensor] = None, eps: float = 1e-5) -> torch.Tensor:
     """LayerNorm of ``x`` over its last dimension; a new tensor like ``x``."""
+    return _layer_norm(x, None, weight, bias, eps)[1]
+
+
+def b200_add_layer_norm(x: torch.Tensor, addend: torch.Tensor,
+                        weight: Optional[torch.Tensor] = None,
+                        bias: Optional[torch.Tensor] = None,
+                        eps: float = 1e-5) -> tuple[torch.Tensor, torch.Tensor]:
+    """``(s, LayerNorm(s))`` for the residual sum ``s = x + addend`` (rounded
+    once to the element type, as a 16-bit tensor add is), in one pass: the
+    residual add that ends one reference block and the norm that starts the
+    next (torch_transformer_benchmark.py:141-142) or the final norm (:170)."""
+    if tuple(addend.shape) != tuple(x.shape):
+        raise ValueError(f"addend must have x's shape {tuple(x.shape)}")
+    if addend.dtype != x.dtype:
+        raise TypeError(f"addend must have x's dtype {x.dtype}, got {addend.dtype}")
+    if addend.device != x.device:
+        raise ValueError("addend must be on x's device")
+    return _layer_norm(x, addend, weight, bias, eps)
+
+
+def _layer_norm(x, addend, weight, bias, eps):
     if x.dim() < 1:
         raise ValueError("x must have at least one dimension")
     cols = x.shape[-1]
@@ -71,19 +94,27 @@ def b200_layer_norm(x: torch.Tensor, weight: Optional[torch.Tensor] = None,
         raise ValueError("eps must be positive")
     w = _vector(weight, cols, "weight", x)
     b = _vector(bias, cols, "bias", x)
-    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (x, weight, bias)):
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad
+                                       for t in (x, addend, weight, bias)):
         raise ValueError("b200_layer_norm is inference-only: it records no autograd graph")
     if not x.is_cuda:
         raise ValueError("b200_layer_norm runs on CUDA tensors only")
     y = torch.empty_like(x, memory_format=torch.contiguous_format)
+    total = torch.empty_like(y) if addend is not None else None
     if y.numel() == 0:
-        return y
+        return total, y
     x2 = _rows(x, cols)
     y2 = y.view(-1, cols)
+    a2 = _rows(addend, cols) if addend is not None else None
+    s2 = total.view(-1, cols) if total is not None else None
     p = _native.LayerNormParams()
     _LN_LAYOUT.pack_into(p, 0, x2.data_ptr(), w.data_ptr() if w is not None else 0,
                          b.data_ptr() if b is not None else 0, y2.data_ptr(), x2.shape[0], cols,
-                         x2.stride(0), y2.stride(0), float(eps), SUPPORTED_DTYPES[x.dtype])
+                         x2.stride(0), y2.stride(0), float(eps), SUPPORTED_DTYPES[x.dtype],
+                         a2.data_ptr() if a2 is not None else 0,
+                         s2.data_ptr() if s2 is not None else 0,
+                         a2.stride(0) if a2 is not None else 0,
+                         s2.stride(0) if s2 is not None else 0)
     lib = _native.load_library()
     rc = lib.b200_layernorm_fwd(ctypes.byref(p),
                                 ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream))
@@ -91,4 +122,4 @@ def b200_layer_norm(x: torch.Tensor, weight: Optional[torch.Tensor] = None,
         raise ValueError(f"b200_layernorm_fwd: {_native.error_text(rc)}")
     if rc != _native.OK:
         raise RuntimeError(f"b200_layernorm_fwd: {_native.error_text(rc)}")
-    return y
+    return total, y

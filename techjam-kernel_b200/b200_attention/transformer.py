@@ -11,13 +11,16 @@ Per block: ``x + attention(norm1(x))`` then ``x + ffn_out(gelu(ffn_in(norm2(x)))
 padded rows zeroed after each block and after the final LayerNorm.
 
 With ``fused_epilogues`` (the default) and the attention on its sm_100a path,
-a block runs its LayerNorms on the B200 LayerNorm kernel (``b200_layer_norm``)
-and the elementwise steps inside the fused linear kernel (``b200_linear``)
+a block runs its LayerNorms on the B200 LayerNorm kernel (``b200_layer_norm``;
+without a padding mask the residual add that ends a block runs in the same pass
+as the next block's first norm, ``b200_add_layer_norm``) and the elementwise
+steps inside the fused linear kernel (``b200_linear``)
 where that measured faster than cuBLAS plus the separate passes at the
 end-to-end shapes: ``out_proj`` with its residual add (and the padded-row
 handling), ``ffn_in`` with the exact GELU, and ``ffn_out`` with its residual
 add and padded-row zeroing when a padding mask is given (without a mask,
-``ffn_out`` is a plain cuBLAS GEMM followed by the add).  The QKV projection
+``ffn_out`` is a plain cuBLAS GEMM whose output is added in that norm pass).
+The QKV projection
 stays one cuBLAS GEMM.  Every rounding point of the unfused sequence is kept.
 An optional
 token embedding in front serves the end-to-end configuration (vocabulary 32000,
@@ -35,7 +38,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .attention_dispatch import AttentionModelSpec
-from .layernorm import b200_layer_norm, layer_norm_supported
+from .layernorm import b200_add_layer_norm, b200_layer_norm, layer_norm_supported
 from .linear import b200_linear, linear_supported
 from .modules import B200FusedSelfAttention
 
@@ -90,14 +93,33 @@ class DecoderBlock(nn.Module):
                 causal: bool) -> torch.Tensor:
         if self._fusable(x):
             h = b200_layer_norm(x, self.norm1.weight, self.norm1.bias, self.norm1.eps)
-            fused = self.attention.residual_forward(h, x, valid_token_mask, causal)
+            fused = self.fused_body(x, h, valid_token_mask, causal)
             if fused is not None:
-                return self._fused_ffn(fused, valid_token_mask)
+                x, pending = fused
+                return x if pending is None else x + pending
         x = x + self.attention(self.norm1(x), valid_token_mask, causal)
         x = x + self.ffn_out(F.gelu(self.ffn_in(self.norm2(x)), approximate="none"))
         if valid_token_mask is not None:
             x = x.masked_fill(~valid_token_mask[..., None], 0)
         return x
+
+    def fused_body(self, x: torch.Tensor, h: torch.Tensor,
+                   valid_token_mask: Optional[torch.Tensor], causal: bool):
+        """The block after its first LayerNorm (``h = norm1(x)``) on the fused
+        kernels.  Returns ``(x_next, pending)``: without a padding mask the last
+        residual add is left ``pending`` (the ffn_out output, to be added to
+        ``x_next`` by the caller, where it can be fused with the next norm);
+        with a mask it is done in ffn_out's epilogue and ``pending`` is None.
+        Returns None when the attention is not on its sm_100a path."""
+        x1 = self.attention.residual_forward(h, x, valid_token_mask, causal)
+        if x1 is None:
+            return None
+        g = b200_layer_norm(x1, self.norm2.weight, self.norm2.bias, self.norm2.eps)
+        g = b200_linear(g, self.ffn_in.weight, self.ffn_in.bias, activation="gelu")
+        if valid_token_mask is None:
+            return x1, self.ffn_out(g)
+        return b200_linear(g, self.ffn_out.weight, self.ffn_out.bias, residual=x1,
+                           row_mask=valid_token_mask, masked_rows="zero"), None
 
     def _fusable(self, x: torch.Tensor) -> bool:
         """The block's LayerNorms and linear layers fit the fused kernels for
@@ -113,14 +135,6 @@ class DecoderBlock(nn.Module):
                 and layer_norm_supported(x, self.norm2.weight)
                 and w.device == x.device and w.dtype == x.dtype
                 and w.shape[0] % 8 == 0 and w.shape[1] % 8 == 0)
-
-    def _fused_ffn(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
-        h = b200_layer_norm(x, self.norm2.weight, self.norm2.bias, self.norm2.eps)
-        h = b200_linear(h, self.ffn_in.weight, self.ffn_in.bias, activation="gelu")
-        if valid_token_mask is None:
-            return x + self.ffn_out(h)
-        return b200_linear(h, self.ffn_out.weight, self.ffn_out.bias, residual=x,
-                           row_mask=valid_token_mask, masked_rows="zero")
 
 
 class Decoder(nn.Module):
@@ -147,17 +161,44 @@ class Decoder(nn.Module):
         model has an embedding."""
         if self.embed is not None and not torch.is_floating_point(x):
             x = self.embed(x)
-        fused = len(self.layers) > 0 and self.layers[0]._fusable(x)
-        for layer in self.layers:
-            x = layer(x, valid_token_mask, self.config.causal)
-        if fused and layer_norm_supported(x, self.final_norm.weight):
-            x = b200_layer_norm(x, self.final_norm.weight, self.final_norm.bias,
-                                self.final_norm.eps)
+        fused = (len(self.layers) > 0 and all(layer._fusable(x) for layer in self.layers)
+                 and layer_norm_supported(x, self.final_norm.weight))
+        if fused:
+            x = self._forward_fused(x, valid_token_mask)
         else:
-            x = self.final_norm(x)
+            x = self._forward_layers(x, valid_token_mask)
         if valid_token_mask is not None:
             x = x.masked_fill(~valid_token_mask[..., None], 0)
         return x
+
+    def _forward_layers(self, x, valid_token_mask):
+        for layer in self.layers:
+            x = layer(x, valid_token_mask, self.config.causal)
+        return self.final_norm(x)
+
+    def _forward_fused(self, x, valid_token_mask):
+        """The blocks on the fused kernels.  Without a padding mask, the
+        residual add that ends each block runs in the same pass as the next
+        block's first LayerNorm (or the final norm): ``b200_add_layer_norm``
+        reads the block's residual stream and its ffn_out output once and
+        writes the rounded sum and its normalisation."""
+        pending = None  # ffn_out output whose residual add with x is still due
+        for layer in self.layers:
+            n1 = layer.norm1
+            if pending is None:
+                h = b200_layer_norm(x, n1.weight, n1.bias, n1.eps)
+            else:
+                x, h = b200_add_layer_norm(x, pending, n1.weight, n1.bias, n1.eps)
+            step = layer.fused_body(x, h, valid_token_mask, self.config.causal)
+            if step is None:  # this layer's attention is not on the sm_100a path
+                x = layer(x, valid_token_mask, self.config.causal)
+                pending = None
+            else:
+                x, pending = step
+        fn = self.final_norm
+        if pending is None:
+            return b200_layer_norm(x, fn.weight, fn.bias, fn.eps)
+        return b200_add_layer_norm(x, pending, fn.weight, fn.bias, fn.eps)[1]
 
 
 def init_normal_(model: nn.Module, std: float = 0.02, seed: Optional[int] = None) -> nn.Module:

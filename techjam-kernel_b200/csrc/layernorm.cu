@@ -10,6 +10,8 @@
 // writes whole contiguous 512-byte segments), the row kept in registers
 // between the mean and variance reductions, so every byte of x is read once
 // and every byte of y written once.  Eight rows per 256-thread block.
+// With an addend, the residual add that precedes the norm in the reference
+// block is done in the same pass (x + addend rounded once, optionally stored).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -38,7 +40,9 @@ struct LnArgs {
   const uint16_t* w;
   const uint16_t* b;
   uint16_t* y;
-  int64_t rows, ldx, ldy;
+  const uint16_t* add;  // addend or null
+  uint16_t* sum;        // x + addend out, or null
+  int64_t rows, ldx, ldy, lda, lds;
   int32_t cols;
   float eps;
 };
@@ -98,7 +102,10 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
 
 // VPL: 16-byte vectors per lane (8 elements each), cols <= 256 * VPL.  The
 // row is widened to fp32 once and kept in registers (4 * VPL pairs per lane).
-template <int VPL, bool BF16>
+// ADD: normalise x + addend (rounded once to the element type), optionally
+// writing that sum; each lane reads its columns in full before it writes
+// them, so the sum may overwrite x in place.
+template <int VPL, bool BF16, bool ADD>
 __global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -107,12 +114,38 @@ __global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
   const uint16_t* xr = a.x + row * a.ldx;
   float2 f[VPL][4];
   float2 s2 = make_float2(0.f, 0.f);
+  uint4 v[VPL];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int col = (i * 32 + lane) * 8;
-    const uint4 v =
-        col < a.cols ? __ldg(reinterpret_cast<const uint4*>(xr + col)) : make_uint4(0u, 0u, 0u, 0u);
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
+    v[i] = col < a.cols ? __ldg(reinterpret_cast<const uint4*>(xr + col)) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  if constexpr (ADD) {
+    const uint16_t* ar = a.add + row * a.lda;
+    uint16_t* sr = a.sum ? a.sum + row * a.lds : nullptr;
+    uint4 tv[VPL];  // every load of the row is in flight before the first add
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int col = (i * 32 + lane) * 8;
+      tv[i] = col < a.cols ? __ldg(reinterpret_cast<const uint4*>(ar + col)) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int col = (i * 32 + lane) * 8;
+      if (col >= a.cols) continue;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&v[i]);
+      const uint32_t* tw = reinterpret_cast<const uint32_t*>(&tv[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 sum = add2(unpack2<BF16>(w[j]), unpack2<BF16>(tw[j]));
+        w[j] = pack2<BF16>(sum.x, sum.y);  // the 16-bit residual sum
+      }
+      if (sr) *reinterpret_cast<uint4*>(sr + col) = v[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[i]);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       f[i][j] = unpack2<BF16>(w[j]);
@@ -159,15 +192,21 @@ __global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+template <bool BF, bool ADD>
+void launch_vpl(const LnArgs& a, unsigned grid, cudaStream_t s) {
+  const int vpl = (a.cols + 255) / 256;
+  if (vpl <= 1) layernorm_kernel<1, BF, ADD><<<grid, kThreads, 0, s>>>(a);
+  else if (vpl <= 2) layernorm_kernel<2, BF, ADD><<<grid, kThreads, 0, s>>>(a);
+  else if (vpl <= 4) layernorm_kernel<4, BF, ADD><<<grid, kThreads, 0, s>>>(a);
+  else if (vpl <= 8) layernorm_kernel<8, BF, ADD><<<grid, kThreads, 0, s>>>(a);
+  else layernorm_kernel<16, BF, ADD><<<grid, kThreads, 0, s>>>(a);
+}
+
 template <bool BF>
 int launch(const LnArgs& a, cudaStream_t s) {
   const unsigned grid = static_cast<unsigned>((a.rows + kRowsPerBlock - 1) / kRowsPerBlock);
-  const int vpl = (a.cols + 255) / 256;
-  if (vpl <= 1) layernorm_kernel<1, BF><<<grid, kThreads, 0, s>>>(a);
-  else if (vpl <= 2) layernorm_kernel<2, BF><<<grid, kThreads, 0, s>>>(a);
-  else if (vpl <= 4) layernorm_kernel<4, BF><<<grid, kThreads, 0, s>>>(a);
-  else if (vpl <= 8) layernorm_kernel<8, BF><<<grid, kThreads, 0, s>>>(a);
-  else layernorm_kernel<16, BF><<<grid, kThreads, 0, s>>>(a);
+  if (a.add) launch_vpl<BF, true>(a, grid, s);
+  else launch_vpl<BF, false>(a, grid, s);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(cudaGetErrorString(e));
@@ -204,6 +243,16 @@ extern "C" int32_t b200_layernorm_check(const b200_layernorm_params* p) {
     return B200_ATTN_ERR_ALIGNMENT;
   if (p->rows > 1 && (p->x_row_stride % 8 != 0 || p->y_row_stride % 8 != 0))
     return B200_ATTN_ERR_ALIGNMENT;
+  if (!p->addend && p->sum) return B200_ATTN_ERR_INVALID_ARGUMENT;  // a sum needs an addend
+  if (p->addend) {
+    if (p->rows > 1 && p->addend_row_stride < p->cols) return B200_ATTN_ERR_INVALID_ARGUMENT;
+    if (p->sum && p->rows > 1 && p->sum_row_stride < p->cols) return B200_ATTN_ERR_INVALID_ARGUMENT;
+    if (p->sum && p->sum == p->y) return B200_ATTN_ERR_INVALID_ARGUMENT;
+    if (!aligned16(p->addend) || (p->sum && !aligned16(p->sum))) return B200_ATTN_ERR_ALIGNMENT;
+    if (p->rows > 1 &&
+        (p->addend_row_stride % 8 != 0 || (p->sum && p->sum_row_stride % 8 != 0)))
+      return B200_ATTN_ERR_ALIGNMENT;
+  }
   return B200_ATTN_OK;
 }
 
@@ -237,6 +286,10 @@ extern "C" int32_t b200_layernorm_fwd(const b200_layernorm_params* p, void* stre
   a.ldx = p->x_row_stride;
   a.ldy = p->y_row_stride;
   a.eps = p->eps;
+  a.add = static_cast<const uint16_t*>(p->addend);
+  a.sum = static_cast<uint16_t*>(p->sum);
+  a.lda = p->addend ? p->addend_row_stride : 0;
+  a.lds = p->sum ? p->sum_row_stride : 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return p->dtype == B200_ATTN_DTYPE_BF16 ? launch<true>(a, s) : launch<false>(a, s);
 }

@@ -63,3 +63,26 @@ def test_strided_input_and_module_semantics():
     torch.cuda.synchronize()
     diff = (y.float() - ref.float()).abs()
     assert bool((diff <= 2.0**-6 * ref.float().abs() + 2.0**-9).all())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(3, 24), (257, 1024), (2, 700, 1024), (33, 4096)])
+def test_add_layer_norm(shape, dtype):
+    """The residual sum is exactly torch's 16-bit add; the norm is that of the
+    rounded sum (the reference normalises the stored 16-bit residual stream)."""
+    from b200_attention.layernorm import b200_add_layer_norm
+
+    g = torch.Generator("cpu").manual_seed(5)
+    cols = shape[-1]
+    x = torch.randn(*shape, generator=g).to(dtype).to(DEV)
+    t = (0.5 * torch.randn(*shape, generator=g)).to(dtype).to(DEV)
+    w = (1 + 0.1 * torch.randn(cols, generator=g)).to(dtype).to(DEV)
+    b = (0.1 * torch.randn(cols, generator=g)).to(dtype).to(DEV)
+    s, y = b200_add_layer_norm(x, t, w, b)
+    s_ref = x + t
+    ref = F.layer_norm(s_ref.float(), (cols,), w.float(), b.float(), 1e-5).to(dtype)
+    torch.cuda.synchronize()
+    assert torch.equal(s, s_ref)
+    rtol, atol = TOL[dtype]
+    diff = (y.float() - ref.float()).abs()
+    assert bool((diff <= rtol * ref.float().abs() + atol).all()), diff.max().item()

@@ -72,6 +72,13 @@ def _params(**kw):
     (dict(x_row_stride=1000), _native.ERR_INVALID_ARGUMENT),
     (dict(y=0x200004), _native.ERR_ALIGNMENT),
     (dict(bias=0x300802), _native.ERR_ALIGNMENT),
+    (dict(addend=0x400000, addend_row_stride=1024), _native.OK),
+    (dict(addend=0x400000, addend_row_stride=1024, sum=0x100000, sum_row_stride=1024), _native.OK),
+    (dict(sum=0x500000, sum_row_stride=1024), _native.ERR_INVALID_ARGUMENT),  # sum without addend
+    (dict(addend=0x400000, addend_row_stride=1024, sum=0x200000, sum_row_stride=1024),
+     _native.ERR_INVALID_ARGUMENT),  # sum onto the normalised output
+    (dict(addend=0x400000, addend_row_stride=1000), _native.ERR_INVALID_ARGUMENT),
+    (dict(addend=0x400008, addend_row_stride=1024), _native.ERR_ALIGNMENT),
 ])
 def test_check(lib, kw, code):
     assert lib.b200_layernorm_check(ctypes.byref(_params(**kw))) == code
@@ -99,6 +106,6 @@ def test_python_argument_errors():
 def test_packed_layout_fills_every_field_in_order():
     from b200_attention.layernorm import _LN_LAYOUT
     p = _native.LayerNormParams()
-    values = [1, 2, 3, 4, 5, 6, 7, 8, 0.5, 9]
+    values = [1, 2, 3, 4, 5, 6, 7, 8, 0.5, 9, 10, 11, 12, 13]
     _LN_LAYOUT.pack_into(p, 0, *values)
     assert [getattr(p, f) for f, _ in _native.LayerNormParams._fields_] == values
