@@ -490,7 +490,8 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
                    "parallelism": f"data-parallel batch split x{world}, no data-path collective",
                    "launch": "CUDA graph of the whole forward" if graph is not None else "eager",
                    "epilogues": ("fused linear kernel: out_proj + residual, ffn_in + GELU "
-                                 "(QKV and ffn_out on cuBLAS); LayerNorm kernel") if fused else
+                                 "(QKV and ffn_out on cuBLAS); LayerNorm kernel with the "
+                                 "blocks' closing residual add folded in") if fused else
                                 "cuBLAS linear layers + separate GELU / add passes; torch LayerNorm",
                    "l2": f"{n_sets} token sets; each forward streams ~0.4 GB of weights and activations (> L2)",
                    "flop_per_step_job": flop_job},
