@@ -9,8 +9,7 @@
 // HBM-bound: one warp per row, 16-byte loads and stores (a warp reads and
 // writes whole contiguous 512-byte segments), the row kept in registers
 // between the mean and variance reductions, so every byte of x is read once
-// and every byte of y written once.  Eight warps per 256-thread block, a grid
-// of a few blocks per SM, each warp looping over rows.
+// and every byte of y written once.  Eight rows per 256-thread block.
 // With an addend, the residual add that precedes the norm in the reference
 // block is done in the same pass (x + addend rounded once, optionally stored).
 #include <cuda_bf16.h>
@@ -33,9 +32,7 @@ namespace b200ln {
 using b200attn::set_error;
 
 constexpr int kRowsPerBlock = 8;
-constexpr int kBlocksPerSm = 8;  // grid cap per SM (the rows beyond it are looped over)
 constexpr int kThreads = 32 * kRowsPerBlock;
-constexpr int kMaxDevices = 64;
 constexpr int kMaxCols = 4096;  // the row stays in registers (16 vectors per lane)
 
 struct LnArgs {
@@ -105,35 +102,39 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
 
 // VPL: 16-byte vectors per lane (8 elements each), cols <= 256 * VPL.  The
 // row is widened to fp32 once and kept in registers (4 * VPL pairs per lane).
-// The row's 16-byte vectors of x (and of the addend) in this lane's columns.
-template <int VPL, bool ADD>
-__device__ __forceinline__ void load_row(const LnArgs& a, int64_t row, int lane, uint4 (&v)[VPL],
-                                         uint4 (&t)[VPL]) {
+// ADD: normalise x + addend (rounded once to the element type), optionally
+// writing that sum; each lane reads its columns in full before it writes
+// them, so the sum may overwrite x in place.
+template <int VPL, bool BF16, bool ADD>
+__global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + warp;
+  if (row >= a.rows) return;
   const uint16_t* xr = a.x + row * a.ldx;
-  const uint16_t* ar = ADD ? a.add + row * a.lda : nullptr;
+  float2 f[VPL][4];
+  float2 s2 = make_float2(0.f, 0.f);
+  uint4 v[VPL];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int col = (i * 32 + lane) * 8;
     v[i] = col < a.cols ? __ldg(reinterpret_cast<const uint4*>(xr + col)) : make_uint4(0u, 0u, 0u, 0u);
-    if constexpr (ADD)
-      t[i] = col < a.cols ? __ldg(reinterpret_cast<const uint4*>(ar + col)) : make_uint4(0u, 0u, 0u, 0u);
   }
-}
-
-// One row from its loaded vectors.  ADD: normalise x + addend (rounded once to
-// the element type), optionally writing that sum; each lane reads its columns
-// in full before it writes them, so the sum may overwrite x in place.
-template <int VPL, bool BF16, bool ADD>
-__device__ __forceinline__ void norm_row(const LnArgs& a, int64_t row, int lane, uint4 (&v)[VPL],
-                                         const uint4 (&t)[VPL]) {
   if constexpr (ADD) {
+    const uint16_t* ar = a.add + row * a.lda;
     uint16_t* sr = a.sum ? a.sum + row * a.lds : nullptr;
+    uint4 tv[VPL];  // every load of the row is in flight before the first add
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int col = (i * 32 + lane) * 8;
+      tv[i] = col < a.cols ? __ldg(reinterpret_cast<const uint4*>(ar + col)) : make_uint4(0u, 0u, 0u, 0u);
+    }
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const int col = (i * 32 + lane) * 8;
       if (col >= a.cols) continue;
       uint32_t* w = reinterpret_cast<uint32_t*>(&v[i]);
-      const uint32_t* tw = reinterpret_cast<const uint32_t*>(&t[i]);
+      const uint32_t* tw = reinterpret_cast<const uint32_t*>(&tv[i]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 sum = add2(unpack2<BF16>(w[j]), unpack2<BF16>(tw[j]));
@@ -142,8 +143,6 @@ __device__ __forceinline__ void norm_row(const LnArgs& a, int64_t row, int lane,
       if (sr) *reinterpret_cast<uint4*>(sr + col) = v[i];
     }
   }
-  float2 f[VPL][4];
-  float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[i]);
@@ -191,40 +190,6 @@ __device__ __forceinline__ void norm_row(const LnArgs& a, int64_t row, int lane,
   }
 }
 
-// Grid-stride over rows, one warp per row at a time.  For rows of up to 1024
-// columns each warp loads its next row before normalising the current one, so
-// two rows of loads are in flight per warp; wider rows keep one (registers).
-template <int VPL, bool BF16, bool ADD>
-__global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
-  constexpr bool kPrefetch = VPL <= 4;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kRowsPerBlock;
-  int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + warp;
-  if (row >= a.rows) return;
-  uint4 v[VPL], t[VPL];
-  load_row<VPL, ADD>(a, row, lane, v, t);
-  while (true) {
-    const int64_t next = row + stride;
-    if constexpr (kPrefetch) {
-      uint4 vn[VPL], tn[VPL];
-      if (next < a.rows) load_row<VPL, ADD>(a, next, lane, vn, tn);
-      norm_row<VPL, BF16, ADD>(a, row, lane, v, t);
-      if (next >= a.rows) break;
-#pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        v[i] = vn[i];
-        if constexpr (ADD) t[i] = tn[i];
-      }
-    } else {
-      norm_row<VPL, BF16, ADD>(a, row, lane, v, t);
-      if (next >= a.rows) break;
-      load_row<VPL, ADD>(a, next, lane, v, t);
-    }
-    row = next;
-  }
-}
-
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 template <bool BF, bool ADD>
@@ -238,11 +203,8 @@ void launch_vpl(const LnArgs& a, unsigned grid, cudaStream_t s) {
 }
 
 template <bool BF>
-int launch(const LnArgs& a, int num_sms, cudaStream_t s) {
-  // enough blocks to fill every SM several times over; warps loop over the rest
-  const int64_t blocks = (a.rows + kRowsPerBlock - 1) / kRowsPerBlock;
-  const int64_t cap = static_cast<int64_t>(num_sms > 0 ? num_sms : 148) * kBlocksPerSm;
-  const unsigned grid = static_cast<unsigned>(blocks < cap ? blocks : cap);
+int launch(const LnArgs& a, cudaStream_t s) {
+  const unsigned grid = static_cast<unsigned>((a.rows + kRowsPerBlock - 1) / kRowsPerBlock);
   if (a.add) launch_vpl<BF, true>(a, grid, s);
   else launch_vpl<BF, false>(a, grid, s);
   const cudaError_t e = cudaGetLastError();
@@ -266,7 +228,9 @@ using namespace b200ln;
 
 extern "C" int32_t b200_layernorm_check(const b200_layernorm_params* p) {
   if (!p || !p->x || !p->y) return B200_ATTN_ERR_INVALID_ARGUMENT;
-  if (p->rows < 1 || p->cols < 1 || p->rows > (1ll << 40)) return B200_ATTN_ERR_INVALID_ARGUMENT;
+  // one block per kRowsPerBlock rows, at most 2^31 - 1 blocks
+  if (p->rows < 1 || p->cols < 1 || p->rows > static_cast<int64_t>(kRowsPerBlock) * 0x7fffffffll)
+    return B200_ATTN_ERR_INVALID_ARGUMENT;
   if (!(p->eps > 0.f) || !std::isfinite(p->eps)) return B200_ATTN_ERR_INVALID_ARGUMENT;
   if (p->dtype != B200_ATTN_DTYPE_BF16 && p->dtype != B200_ATTN_DTYPE_FP16)
     return B200_ATTN_ERR_UNSUPPORTED;
@@ -326,17 +290,6 @@ extern "C" int32_t b200_layernorm_fwd(const b200_layernorm_params* p, void* stre
   a.sum = static_cast<uint16_t*>(p->sum);
   a.lda = p->addend ? p->addend_row_stride : 0;
   a.lds = p->sum ? p->sum_row_stride : 0;
-  static std::once_flag once[kMaxDevices];
-  static int sms[kMaxDevices];
-  const int dev = attr.device;
-  if (dev < kMaxDevices)
-    std::call_once(once[dev], [dev] {
-      if (cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
-        cudaGetLastError();
-        sms[dev] = 0;
-      }
-    });
-  const int num_sms = dev < kMaxDevices ? sms[dev] : 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return p->dtype == B200_ATTN_DTYPE_BF16 ? launch<true>(a, num_sms, s) : launch<false>(a, num_sms, s);
+  return p->dtype == B200_ATTN_DTYPE_BF16 ? launch<true>(a, s) : launch<false>(a, s);
 }

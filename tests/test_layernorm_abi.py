@@ -63,7 +63,7 @@ def _params(**kw):
     (dict(rows=1, x_row_stride=0), _native.OK),
     (dict(x=None), _native.ERR_INVALID_ARGUMENT),
     (dict(rows=0), _native.ERR_INVALID_ARGUMENT),
-    (dict(rows=(1 << 40) + 1), _native.ERR_INVALID_ARGUMENT),
+    (dict(rows=8 * 0x7fffffff + 1), _native.ERR_INVALID_ARGUMENT),
     (dict(eps=0.0), _native.ERR_INVALID_ARGUMENT),
     (dict(eps=float("nan")), _native.ERR_INVALID_ARGUMENT),
     (dict(dtype=3), _native.ERR_UNSUPPORTED),
