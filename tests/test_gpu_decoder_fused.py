@@ -68,3 +68,27 @@ def test_autograd_takes_the_unfused_path():
     out = fused(x)
     out.float().sum().backward()
     assert x.grad is not None and torch.isfinite(x.grad.float()).all()
+
+
+@pytest.mark.parametrize("padded", [False, True])
+def test_fused_path_never_falls_back_to_torch_norm_or_gelu(padded, monkeypatch):
+    """The reference's fake-fallback detector (test/test_triton_fused_attention.py:124-138):
+    with torch's LayerNorm and GELU made to raise, the fused decoder must still
+    run, so none of its norms or activations silently took the torch path."""
+    import torch.nn.functional as F
+
+    fused, _ = _pair(CFG)
+    x = torch.randn(CFG.batch_size, CFG.seq_len, CFG.d_model, device=DEV, dtype=torch.bfloat16)
+    mask = None
+    if padded:
+        mask = (torch.arange(CFG.seq_len)[None, :] < torch.tensor([CFG.seq_len, 100])[:, None]).to(DEV)
+
+    def forbidden(*args, **kwargs):
+        raise AssertionError("torch fallback used on the fused path")
+
+    monkeypatch.setattr(F, "layer_norm", forbidden)
+    monkeypatch.setattr(F, "gelu", forbidden)
+    with torch.inference_mode():
+        out = fused(x, mask)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
