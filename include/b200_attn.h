@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define B200_ATTN_ABI_VERSION 1
+#define B200_ATTN_ABI_VERSION 2
 
 /* Element types of q, k, v and the output. */
 enum {
@@ -51,7 +51,12 @@ enum {
   B200_ATTN_ERR_ALIGNMENT = 3,        /* base or stride not 16-byte aligned            */
   B200_ATTN_ERR_DEVICE = 4,           /* no sm_100 device, or pointer not on a device  */
   B200_ATTN_ERR_LAUNCH = 5,           /* CUDA launch / tensor-map encoding failed      */
-  B200_ATTN_ERR_TIMEOUT = 6           /* device reported a pipeline wait timeout      */
+  B200_ATTN_ERR_TIMEOUT = 6,          /* an earlier launch reported a pipeline wait
+                                         timeout in the (host) error word; nothing
+                                         was launched                                */
+  B200_ATTN_ERR_DEVICE_BOUNDS = 7     /* an earlier launch reported a failed bounds
+                                         check (checked build) in the (host) error
+                                         word; nothing was launched                  */
 };
 
 /* Bits the kernel ORs into *error_word (when error_word != NULL). */
@@ -83,8 +88,23 @@ typedef struct b200_attn_fwd_params {
   int32_t dtype;           /* B200_ATTN_DTYPE_* */
   int32_t causal;          /* 1: key j visible to query i iff j <= i (top-left aligned) */
   int32_t zero_masked_queries; /* 1: rows whose own mask bit is 0 are written as 0 */
-  int32_t* error_word;     /* optional device int; kernel ORs B200_ATTN_DEVERR_* */
+  int32_t* error_word;     /* optional int32 the kernel reports B200_ATTN_DEVERR_* bits in
+                              (see "Error word" below) */
 } b200_attn_fwd_params;
+
+/* Error word.  `error_word` (here and in the linear and softmax params) is
+ * NULL, a device int32, or a pinned host int32 the device addresses directly
+ * (cudaHostAlloc, or any pinned allocation under unified addressing).
+ *   - device word: kernels OR their B200_ATTN_DEVERR_* bits in atomically; the
+ *     caller reads it after synchronising.
+ *   - host word: the caller can read it at any time without synchronising.
+ *     Every entry point reads it before launching and, while it is non-zero,
+ *     launches nothing and returns B200_ATTN_ERR_TIMEOUT (timeout bit set) or
+ *     B200_ATTN_ERR_DEVICE_BOUNDS; the caller clears it (writes 0) once it has
+ *     handled the report.  Kernels write a host word with plain stores, so two
+ *     CTAs reporting at once may keep only one CTA's bits; a report never
+ *     leaves the word zero.
+ * A launch whose kernel reported an error has undefined output. */
 
 /* ABI version (B200_ATTN_ABI_VERSION). */
 B200_ATTN_API int32_t b200_attn_abi_version(void);
@@ -121,6 +141,23 @@ B200_ATTN_API int32_t b200_attn_launches_per_call(const b200_attn_fwd_params* p)
 /* Text of the last host-side failure on the calling thread (CUDA error string,
  * tensor-map encoding failure); empty when none. */
 B200_ATTN_API const char* b200_attn_last_error_detail(void);
+
+/* Kernel launches issued so far by every entry point of this library in this
+ * process (attention, linear, LayerNorm, softmax), counted on the host after
+ * each successful launch (no reference counterpart; benchmarks count their
+ * launches with it).  Launches replayed from a CUDA graph are counted once, at
+ * capture. */
+B200_ATTN_API int64_t b200_attn_launch_count(void);
+
+/* Launch shape of the kernel instance b200_attn_fwd runs for (dtype,
+ * head_dim), host-only: query rows per tensor-memory tile, query rows per CTA,
+ * keys per K/V tile, warps per CTA and K/V ring slots (one K or one V tile per
+ * slot).  Returns 1 and fills the outputs when the pair is supported, else 0.
+ * Replaces the launch metadata the reference planner attaches to its plans
+ * (model/attention_dispatch.py:303-354). */
+B200_ATTN_API int32_t b200_attn_launch_shape(int32_t dtype, int64_t head_dim, int32_t* block_m,
+                                             int32_t* rows_per_cta, int32_t* block_n,
+                                             int32_t* num_warps, int32_t* ring_slots);
 
 /* Self-test of failure detection (no reference counterpart).  Launches the
  * forward exactly like b200_attn_fwd, except that in every CTA the K/V load

@@ -32,7 +32,7 @@ typedef struct b200_layernorm_params {
   const void* x;          /* [rows, cols] */
   const void* weight;     /* [cols] or NULL */
   const void* bias;       /* [cols] or NULL */
-  void* y;                /* [rows, cols], may be x itself */
+  void* y;                /* [rows, cols]; may be x (or the addend) itself */
   int64_t rows;
   int64_t cols;           /* multiple of 8, at most 4096 */
   int64_t x_row_stride;   /* elements */
@@ -40,13 +40,16 @@ typedef struct b200_layernorm_params {
   float eps;              /* > 0 */
   int32_t dtype;          /* B200_ATTN_DTYPE_* */
   const void* addend;     /* [rows, cols] or NULL: normalise x + addend */
-  void* sum;              /* [rows, cols] or NULL: receives x + addend (may be x itself) */
+  void* sum;              /* [rows, cols] or NULL: receives x + addend (may be x or the
+                             addend itself, never y) */
   int64_t addend_row_stride;
   int64_t sum_row_stride;
 } b200_layernorm_params;
 
 /* Host-only validation (sizes, dtype, eps, 16-byte alignment of bases and row
- * strides).  Makes no CUDA call.  Replaces the shape checks of
+ * strides, and aliasing: an output may be exactly an input -- the same base
+ * and row stride -- but any other overlap of an output with an input, or of y
+ * with sum, returns B200_ATTN_ERR_INVALID_ARGUMENT).  Makes no CUDA call.  Replaces the shape checks of
  * torch.nn.functional.layer_norm for these calls. */
 B200_ATTN_API int32_t b200_layernorm_check(const b200_layernorm_params* p);
 

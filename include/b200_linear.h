@@ -52,7 +52,8 @@ typedef struct b200_linear_params {
   const void* bias;         /* [N] or NULL */
   const void* residual;     /* [M, N] or NULL */
   const uint8_t* row_mask;  /* [M] bytes, 1 = valid row; NULL = every row valid */
-  void* y;                  /* [M, N] output, must not overlap the inputs */
+  void* y;                  /* [M, N] output; its bytes must not overlap any input's
+                               (b200_linear_check returns B200_ATTN_ERR_INVALID_ARGUMENT) */
   int64_t m;
   int64_t n;
   int64_t k;
@@ -64,11 +65,16 @@ typedef struct b200_linear_params {
   int32_t activation;       /* B200_LINEAR_ACT_* */
   int32_t masked_rows;      /* B200_LINEAR_MASKED_*; used only with row_mask */
   int32_t reserved;         /* 0 */
-  int32_t* error_word;      /* optional device int; kernel ORs B200_ATTN_DEVERR_* */
+  int32_t* error_word;      /* optional int32 the kernel reports B200_ATTN_DEVERR_* bits in:
+                               a device word or a pinned host word (see "Error word" in
+                               b200_attn.h; a host word that holds a report makes
+                               b200_linear_fwd return B200_ATTN_ERR_TIMEOUT / _DEVICE_BOUNDS
+                               without launching) */
 } b200_linear_params;
 
 /* Host-only validation (sizes, dtype, flags, 16-byte alignment of every base
- * and row stride, N and K multiples of 8).  Makes no CUDA call.  Replaces the
+ * and row stride, N and K multiples of 8, y disjoint from every input).  Makes
+ * no CUDA call.  Replaces the
  * shape checks torch's nn.Linear applies to these calls. */
 B200_ATTN_API int32_t b200_linear_check(const b200_linear_params* p);
 

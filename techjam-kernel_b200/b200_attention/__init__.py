@@ -7,5 +7,6 @@
   (bias, exact GELU, residual add, padded-row zeroing) fused into one kernel
 """
 
-from .fused_attention import b200_fused_attention, read_device_errors  # noqa: F401
+from .fused_attention import (DeviceError, b200_fused_attention, check_device_errors,  # noqa: F401
+                              clear_device_errors, read_device_errors)
 from .linear import b200_linear  # noqa: F401

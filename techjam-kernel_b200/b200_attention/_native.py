@@ -24,6 +24,10 @@ ERR_ALIGNMENT = 3
 ERR_DEVICE = 4
 ERR_LAUNCH = 5
 ERR_TIMEOUT = 6
+ERR_DEVICE_BOUNDS = 7
+# codes with which an entry point refuses to launch because the (host) error
+# word still holds an earlier launch's report
+DEVICE_REPORT_CODES = (ERR_TIMEOUT, ERR_DEVICE_BOUNDS)
 
 DEVERR_WAIT_TIMEOUT = 1
 DEVERR_BOUNDS = 2
@@ -38,6 +42,8 @@ EXPORTED_SYMBOLS = (
     "b200_attn_launches_per_call",
     "b200_attn_last_error_detail",
     "b200_attn_selftest_stall",
+    "b200_attn_launch_count",
+    "b200_attn_launch_shape",
 )
 # Every symbol ``include/b200_linear.h`` declares.
 LINEAR_SYMBOLS = (
@@ -150,6 +156,11 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.b200_attn_launches_per_call.argtypes = [ctypes.POINTER(FwdParams)]
     lib.b200_attn_last_error_detail.restype = ctypes.c_char_p
     lib.b200_attn_last_error_detail.argtypes = []
+    lib.b200_attn_launch_count.restype = ctypes.c_int64
+    lib.b200_attn_launch_count.argtypes = []
+    lib.b200_attn_launch_shape.restype = ctypes.c_int32
+    lib.b200_attn_launch_shape.argtypes = [ctypes.c_int32, ctypes.c_int64] + [
+        ctypes.POINTER(ctypes.c_int32)] * 5
     lib.b200_attn_selftest_stall.restype = ctypes.c_int32
     lib.b200_attn_selftest_stall.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_int32,
                                              ctypes.c_void_p]
@@ -196,3 +207,18 @@ def error_text(code: int) -> str:
     text = lib.b200_attn_error_string(int(code)).decode()
     detail = lib.b200_attn_last_error_detail().decode()
     return f"{text} ({detail})" if detail and code in (ERR_DEVICE, ERR_LAUNCH) else text
+
+
+def launch_count() -> int:
+    """Kernel launches this library has issued in this process (all entry points)."""
+    return int(load_library().b200_attn_launch_count())
+
+
+def launch_shape(dtype: int, head_dim: int) -> dict | None:
+    """The attention kernel's launch shape for (dtype, head_dim), from the C ABI."""
+    vals = [ctypes.c_int32() for _ in range(5)]
+    if not load_library().b200_attn_launch_shape(int(dtype), int(head_dim),
+                                                 *[ctypes.byref(v) for v in vals]):
+        return None
+    names = ("block_m", "rows_per_cta", "block_n", "num_warps", "ring_slots")
+    return {n: v.value for n, v in zip(names, vals)}

@@ -82,6 +82,20 @@ SM100_DTYPES = ("bfloat16", "float16")
 # instance with the missing columns read as zeros by TMA.
 SM100_HEAD_DIMS = tuple(range(8, 129, 8))
 SM100_CAPABILITY_MAJOR = 10
+# Launch shape of the sm_100a kernel (the C ABI's b200_attn_launch_shape
+# reports the same values; a CPU test keeps the two in agreement): 128-row
+# query tiles, two per CTA, 128-key K/V tiles, 11 warps (two softmax
+# warpgroups, a TMA warp and two tcgen05 issuer warps), and a ring of K/V
+# slots (one K or one V tile each) whose depth depends on the instance.
+SM100_BLOCK_M = 128
+SM100_BLOCK_N = 128
+SM100_NUM_WARPS = 11
+
+
+def sm100_ring_slots(head_dim: int) -> int:
+    """K/V ring slots of the kernel instance that serves ``head_dim``: the
+    64-wide instance (head dims up to 64) holds 10, the 128-wide one 5."""
+    return 10 if head_dim <= 64 else 5
 
 
 @dataclass(frozen=True, slots=True)
@@ -247,10 +261,9 @@ def _rule_matches(rule: tuple, spec: AttentionModelSpec, dtype: str) -> bool:
 
 
 def _sm100_launch(head_dim: int) -> KernelLaunch:
-    # 128x128 tiles, 10 warps (2 softmax warpgroups, TMA warp, MMA warp);
-    # num_stages = K/V tile pairs resident in the shared-memory ring.
-    return KernelLaunch(block_m=128, block_n=128, num_warps=10,
-                        num_stages=2 if head_dim == 128 else 3, output_layout="bshd")
+    # num_stages = K/V ring slots (one K or one V tile per slot)
+    return KernelLaunch(block_m=SM100_BLOCK_M, block_n=SM100_BLOCK_N, num_warps=SM100_NUM_WARPS,
+                        num_stages=sm100_ring_slots(head_dim), output_layout="bshd")
 
 
 def _published_launch(mode: AttentionMode, spec: AttentionModelSpec) -> Optional[KernelLaunch]:

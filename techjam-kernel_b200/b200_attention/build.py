@@ -26,7 +26,7 @@ LIB_PATH = PACKAGE_DIR / LIB_NAME
 CHECKED_LIB_PATH = PACKAGE_DIR / "libb200_attention_checked.so"
 
 SOURCES = ("attn_fwd_sm100.cu", "linear_sm100.cu", "layernorm.cu")
-HEADERS = ("sm100_ptx.cuh",)
+HEADERS = ("sm100_ptx.cuh", "error_word.cuh", "byte_range.h")
 
 NVCC_FLAGS = (
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -108,8 +108,28 @@ def _capability_major(device: torch.device) -> int:
     return major
 
 
+class DeviceError(RuntimeError):
+    """A kernel launched earlier on this device reported an error (a pipeline
+    wait that ran out, or a failed bounds check in the checked build) in the
+    device's error word.  The outputs of that launch are undefined; every later
+    launch on the device is refused until ``clear_device_errors`` is called."""
+
+
+_DEVERR_NAMES = {_native.DEVERR_WAIT_TIMEOUT: "pipeline wait timeout",
+                 _native.DEVERR_BOUNDS: "failed bounds check"}
+
+
+def _describe(bits: int) -> str:
+    names = [name for bit, name in _DEVERR_NAMES.items() if bits & bit]
+    return ", ".join(names) or f"error bits {bits:#x}"
+
+
 def device_error_word(device: torch.device) -> torch.Tensor:
-    """Per-device int32 the kernel ORs error bits into (allocated once)."""
+    """Per-device int32 error word that every kernel of this package reports
+    into (allocated once).  It lives in pinned host memory the device
+    addresses directly, so the host can read it without synchronising: each
+    entry point checks it before launching and refuses to launch while it
+    holds a report (``include/b200_attn.h``, "Error word")."""
     index = device.index if device.index is not None else torch.cuda.current_device()
     word = _error_words.get(index)
     if word is None:
@@ -117,20 +137,52 @@ def device_error_word(device: torch.device) -> torch.Tensor:
             word = _error_words.get(index)
             if word is None:
                 # a normal tensor even when the first call runs under
-                # torch.inference_mode(), so read_device_errors can clear it anywhere
+                # torch.inference_mode(), so the word can be cleared anywhere
                 with torch.inference_mode(False):
-                    word = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+                    word = torch.zeros(1, dtype=torch.int32, pin_memory=True)
                 _error_words[index] = word
     return word
 
 
 def read_device_errors(device: torch.device, clear: bool = True) -> int:
-    """Synchronise and return the error bits the kernel reported on ``device``."""
+    """Synchronise ``device`` and return the error bits its kernels reported
+    (clearing them unless ``clear`` is False)."""
     word = device_error_word(device)
-    value = int(word.item())
+    torch.cuda.synchronize(device)
+    value = int(word[0])
     if clear and value:
         word.zero_()
     return value
+
+
+def clear_device_errors(device: torch.device) -> None:
+    """Synchronise ``device`` and clear its error word (launches resume)."""
+    read_device_errors(device, clear=True)
+
+
+def check_device_errors(device: torch.device) -> None:
+    """Raise ``DeviceError`` when a launch that already finished on ``device``
+    reported an error.  Reads the host-side word only: no synchronisation,
+    safe inside CUDA graph capture."""
+    value = int(device_error_word(device)[0])
+    if value:
+        raise DeviceError(f"a kernel on {device} reported a {_describe(value)}; its output is "
+                          "undefined (clear_device_errors resumes launches)")
+
+
+def raise_for_code(entry: str, rc: int, device: torch.device) -> None:
+    """Turn a nonzero C-ABI return code into the exception the reference's
+    operator raises for it (``ValueError`` for contract violations)."""
+    if rc in (_native.ERR_INVALID_ARGUMENT, _native.ERR_ALIGNMENT):
+        raise ValueError(f"{entry}: {_native.error_text(rc)}")
+    if rc == _native.ERR_UNSUPPORTED:
+        raise ValueError(f"unsupported sm_100a invocation ({entry}): {_native.error_text(rc)}")
+    if rc in _native.DEVICE_REPORT_CODES:
+        value = int(device_error_word(device)[0])
+        raise DeviceError(f"{entry} refused to launch: an earlier kernel on {device} reported a "
+                          f"{_describe(value)}; its output is undefined "
+                          "(clear_device_errors resumes launches)")
+    raise RuntimeError(f"{entry}: {_native.error_text(rc)}")
 
 
 def _strides(t: torch.Tensor) -> tuple[int, int, int]:
@@ -239,10 +291,6 @@ def b200_fused_attention(
     )
     stream = torch.cuda.current_stream(q.device).cuda_stream
     rc = lib.b200_attn_fwd(ctypes.byref(params), ctypes.c_void_p(stream))
-    if rc == _native.ERR_INVALID_ARGUMENT or rc == _native.ERR_ALIGNMENT:
-        raise ValueError(f"b200_attn_fwd: {_native.error_text(rc)}")
-    if rc == _native.ERR_UNSUPPORTED:
-        raise ValueError(f"unsupported sm_100a attention invocation: {_native.error_text(rc)}")
     if rc != _native.OK:
-        raise RuntimeError(f"b200_attn_fwd: {_native.error_text(rc)}")
+        raise_for_code("b200_attn_fwd", rc, q.device)
     return out

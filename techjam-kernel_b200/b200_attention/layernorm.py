@@ -19,7 +19,7 @@ from typing import Optional
 import torch
 
 from . import _native
-from .fused_attention import SUPPORTED_DTYPES
+from .fused_attention import SUPPORTED_DTYPES, raise_for_code
 
 MAX_COLS = 4096
 
@@ -37,8 +37,12 @@ def layer_norm_supported(x: torch.Tensor, weight: Optional[torch.Tensor]) -> boo
 
 
 def _rows(t: torch.Tensor, cols: int) -> torch.Tensor:
+    """``t`` as a 2-D [rows, cols] view with a contiguous last dim and
+    non-overlapping rows whose stride is a multiple of 8 elements (copied only
+    when no such view exists, e.g. for a broadcast ``expand``)."""
     flat = t.reshape(-1, cols)
-    if (flat.stride(-1) != 1 or (flat.shape[0] > 1 and flat.stride(0) % 8 != 0)
+    if (flat.stride(-1) != 1
+            or (flat.shape[0] > 1 and (flat.stride(0) % 8 != 0 or flat.stride(0) < cols))
             or flat.data_ptr() % 16 != 0):
         flat = flat.contiguous()
     return flat
@@ -118,8 +122,6 @@ def _layer_norm(x, addend, weight, bias, eps):
     lib = _native.load_library()
     rc = lib.b200_layernorm_fwd(ctypes.byref(p),
                                 ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream))
-    if rc in (_native.ERR_INVALID_ARGUMENT, _native.ERR_ALIGNMENT, _native.ERR_UNSUPPORTED):
-        raise ValueError(f"b200_layernorm_fwd: {_native.error_text(rc)}")
     if rc != _native.OK:
-        raise RuntimeError(f"b200_layernorm_fwd: {_native.error_text(rc)}")
+        raise_for_code("b200_layernorm_fwd", rc, x.device)
     return total, y

@@ -29,7 +29,7 @@ from typing import Optional
 import torch
 
 from . import _native
-from .fused_attention import SUPPORTED_DTYPES, device_error_word
+from .fused_attention import SUPPORTED_DTYPES, device_error_word, raise_for_code
 
 # b200_linear_params packed in one call (layout checked against the ctypes
 # mirror at import): six pointers, m n k, four row strides, dtype, activation,
@@ -53,10 +53,12 @@ def linear_supported(x: torch.Tensor, weight: torch.Tensor) -> bool:
 
 
 def _rows(t: torch.Tensor, cols: int) -> torch.Tensor:
-    """``t`` as a 2-D [rows, cols] view with a contiguous last dim (copied only
-    when no such view exists)."""
+    """``t`` as a 2-D [rows, cols] view with a contiguous last dim and
+    non-overlapping rows whose stride is a multiple of 8 elements (copied only
+    when no such view exists, e.g. for a broadcast ``expand``)."""
     flat = t.reshape(-1, cols)
-    if (flat.stride(-1) != 1 or (flat.shape[0] > 1 and flat.stride(0) % 8 != 0)
+    if (flat.stride(-1) != 1
+            or (flat.shape[0] > 1 and (flat.stride(0) % 8 != 0 or flat.stride(0) < cols))
             or flat.data_ptr() % 16 != 0):
         flat = flat.contiguous()
     return flat
@@ -138,8 +140,6 @@ def b200_linear(
     lib = _native.load_library()
     stream = torch.cuda.current_stream(x.device).cuda_stream
     rc = lib.b200_linear_fwd(ctypes.byref(p), ctypes.c_void_p(stream))
-    if rc in (_native.ERR_INVALID_ARGUMENT, _native.ERR_ALIGNMENT, _native.ERR_UNSUPPORTED):
-        raise ValueError(f"b200_linear_fwd: {_native.error_text(rc)}")
     if rc != _native.OK:
-        raise RuntimeError(f"b200_linear_fwd: {_native.error_text(rc)}")
+        raise_for_code("b200_linear_fwd", rc, x.device)
     return y

@@ -43,10 +43,12 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
 #include "b200_attn.h"
+#include "error_word.cuh"
 #include "sm100_ptx.cuh"
 
 namespace b200attn {
@@ -116,7 +118,7 @@ struct KernelArgs {
   int64_t mask_ss;
   void* o;               // output base (for zero rows of skipped blocks)
   int64_t o_sb, o_sh, o_ss;  // elements
-  int32_t* err;
+  int32_t* err;          // error word as resolve_error_word returns it (bit 0: host word)
   int32_t skip_load;     // stall self-test only: K/V load left out (see b200_attn_selftest_stall)
 };
 
@@ -276,7 +278,7 @@ __device__ __noinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity,
     if (*abort_flag) return false;
     if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
       *abort_flag = 1u;
-      if (err) atomicOr(err, B200_ATTN_DEVERR_WAIT_TIMEOUT);
+      report_error(err, B200_ATTN_DEVERR_WAIT_TIMEOUT);
       return false;
     }
   }
@@ -408,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto chk = [&](bool cond) {
     if constexpr (kChecked) {
       if (!cond) {
-        if (args.err) atomicOr(args.err, B200_ATTN_DEVERR_BOUNDS);
+        report_error(args.err, B200_ATTN_DEVERR_BOUNDS);
         *abort_flag = 1u;
       }
       return cond;
@@ -973,6 +975,10 @@ void set_error(const char* msg) {
   std::snprintf(g_last_error, sizeof(g_last_error), "%s", msg);
 }
 
+std::atomic<int64_t> g_launch_count{0};
+
+void count_launch() { g_launch_count.fetch_add(1, std::memory_order_relaxed); }
+
 namespace {
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1070,6 +1076,7 @@ int launch_one(const CUtensorMap maps[4], const KernelArgs& args, int device, cu
     set_error(cudaGetErrorString(e));
     return B200_ATTN_ERR_LAUNCH;
   }
+  count_launch();
   return B200_ATTN_OK;
 }
 
@@ -1113,12 +1120,31 @@ extern "C" const char* b200_attn_error_string(int32_t code) {
     case B200_ATTN_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned";
     case B200_ATTN_ERR_DEVICE: return "no sm_100 device for the given pointers";
     case B200_ATTN_ERR_LAUNCH: return "kernel launch failed";
-    case B200_ATTN_ERR_TIMEOUT: return "device pipeline wait timed out";
+    case B200_ATTN_ERR_TIMEOUT: return "an earlier launch reported a device pipeline wait timeout";
+    case B200_ATTN_ERR_DEVICE_BOUNDS:
+      return "an earlier launch reported a failed device bounds check";
     default: return "unknown error";
   }
 }
 
 extern "C" const char* b200_attn_last_error_detail(void) { return g_last_error; }
+
+extern "C" int64_t b200_attn_launch_count(void) {
+  return g_launch_count.load(std::memory_order_relaxed);
+}
+
+extern "C" int32_t b200_attn_launch_shape(int32_t dtype, int64_t head_dim, int32_t* block_m,
+                                          int32_t* rows_per_cta, int32_t* block_n,
+                                          int32_t* num_warps, int32_t* ring_slots) {
+  if (!b200_attn_query(dtype, head_dim, 0, 0)) return 0;
+  const bool wide = wide_head(head_dim);
+  if (block_m) *block_m = kBlockM;
+  if (rows_per_cta) *rows_per_cta = kRowsPerCta;
+  if (block_n) *block_n = wide ? Cfg128::BN : Cfg64::BN;
+  if (num_warps) *num_warps = kThreads / 32;
+  if (ring_slots) *ring_slots = wide ? Cfg128::NSLOT : Cfg64::NSLOT;
+  return 1;
+}
 
 extern "C" int32_t b200_attn_check(const b200_attn_fwd_params* p) {
   if (!p || !p->q || !p->k || !p->v || !p->o) return B200_ATTN_ERR_INVALID_ARGUMENT;
@@ -1220,7 +1246,7 @@ int32_t prepare(const b200_attn_fwd_params* p, CUtensorMap maps[4], KernelArgs& 
   a.o_sb = p->o_stride[0];
   a.o_sh = p->o_stride[1];
   a.o_ss = p->o_stride[2];
-  a.err = p->error_word;
+  if ((rc = resolve_error_word(p->error_word, &a.err)) != B200_ATTN_OK) return rc;
   a.skip_load = -1;
   if (static_cast<int64_t>(a.num_q_blocks) * p->batch * p->heads > 0x7fffffffll)
     return B200_ATTN_ERR_INVALID_ARGUMENT;

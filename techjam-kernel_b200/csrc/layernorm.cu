@@ -21,14 +21,14 @@
 #include <mutex>
 
 #include "b200_layernorm.h"
-
-namespace b200attn {
-// Records the text b200_attn_last_error_detail returns (attn_fwd_sm100.cu).
-void set_error(const char* msg);
-}  // namespace b200attn
+#include "byte_range.h"
+#include "error_word.cuh"
 
 namespace b200ln {
 
+using b200attn::ByteRange;
+using b200attn::count_launch;
+using b200attn::rows_range;
 using b200attn::set_error;
 
 constexpr int kRowsPerBlock = 8;
@@ -100,12 +100,25 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   return d;
 }
 
+// 16 bytes of a row: through the non-coherent (read-only) path when no
+// output of the launch aliases the row's tensor, else a plain global load.
+template <bool NC>
+__device__ __forceinline__ uint4 load16(const uint16_t* p) {
+  if constexpr (NC) {
+    return __ldg(reinterpret_cast<const uint4*>(p));
+  } else {
+    return *reinterpret_cast<const uint4*>(p);
+  }
+}
+
 // VPL: 16-byte vectors per lane (8 elements each), cols <= 256 * VPL.  The
 // row is widened to fp32 once and kept in registers (4 * VPL pairs per lane).
 // ADD: normalise x + addend (rounded once to the element type), optionally
 // writing that sum; each lane reads its columns in full before it writes
-// them, so the sum may overwrite x in place.
-template <int VPL, bool BF16, bool ADD>
+// them, so y or the sum may overwrite x in place.  NC: x and the addend stay
+// read-only for the whole launch (no output aliases them), so they may be
+// read through the non-coherent path.
+template <int VPL, bool BF16, bool ADD, bool NC>
 __global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -118,7 +131,7 @@ __global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int col = (i * 32 + lane) * 8;
-    v[i] = col < a.cols ? __ldg(reinterpret_cast<const uint4*>(xr + col)) : make_uint4(0u, 0u, 0u, 0u);
+    v[i] = col < a.cols ? load16<NC>(xr + col) : make_uint4(0u, 0u, 0u, 0u);
   }
   if constexpr (ADD) {
     const uint16_t* ar = a.add + row * a.lda;
@@ -127,7 +140,7 @@ __global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const int col = (i * 32 + lane) * 8;
-      tv[i] = col < a.cols ? __ldg(reinterpret_cast<const uint4*>(ar + col)) : make_uint4(0u, 0u, 0u, 0u);
+      tv[i] = col < a.cols ? load16<NC>(ar + col) : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
@@ -192,27 +205,67 @@ __global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <bool BF, bool ADD>
+template <bool BF, bool ADD, bool NC>
 void launch_vpl(const LnArgs& a, unsigned grid, cudaStream_t s) {
   const int vpl = (a.cols + 255) / 256;
-  if (vpl <= 1) layernorm_kernel<1, BF, ADD><<<grid, kThreads, 0, s>>>(a);
-  else if (vpl <= 2) layernorm_kernel<2, BF, ADD><<<grid, kThreads, 0, s>>>(a);
-  else if (vpl <= 4) layernorm_kernel<4, BF, ADD><<<grid, kThreads, 0, s>>>(a);
-  else if (vpl <= 8) layernorm_kernel<8, BF, ADD><<<grid, kThreads, 0, s>>>(a);
-  else layernorm_kernel<16, BF, ADD><<<grid, kThreads, 0, s>>>(a);
+  if (vpl <= 1) layernorm_kernel<1, BF, ADD, NC><<<grid, kThreads, 0, s>>>(a);
+  else if (vpl <= 2) layernorm_kernel<2, BF, ADD, NC><<<grid, kThreads, 0, s>>>(a);
+  else if (vpl <= 4) layernorm_kernel<4, BF, ADD, NC><<<grid, kThreads, 0, s>>>(a);
+  else if (vpl <= 8) layernorm_kernel<8, BF, ADD, NC><<<grid, kThreads, 0, s>>>(a);
+  else layernorm_kernel<16, BF, ADD, NC><<<grid, kThreads, 0, s>>>(a);
 }
 
 template <bool BF>
-int launch(const LnArgs& a, cudaStream_t s) {
+int launch(const LnArgs& a, bool in_place, cudaStream_t s) {
   const unsigned grid = static_cast<unsigned>((a.rows + kRowsPerBlock - 1) / kRowsPerBlock);
-  if (a.add) launch_vpl<BF, true>(a, grid, s);
-  else launch_vpl<BF, false>(a, grid, s);
+  if (a.add) {
+    if (in_place) launch_vpl<BF, true, false>(a, grid, s);
+    else launch_vpl<BF, true, true>(a, grid, s);
+  } else {
+    if (in_place) launch_vpl<BF, false, false>(a, grid, s);
+    else launch_vpl<BF, false, true>(a, grid, s);
+  }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(cudaGetErrorString(e));
     return B200_ATTN_ERR_LAUNCH;
   }
+  count_launch();
   return B200_ATTN_OK;
+}
+
+ByteRange x_range(const b200_layernorm_params* p) {
+  return rows_range(p->x, p->rows, p->cols, p->x_row_stride);
+}
+ByteRange y_range(const b200_layernorm_params* p) {
+  return rows_range(p->y, p->rows, p->cols, p->y_row_stride);
+}
+ByteRange add_range(const b200_layernorm_params* p) {
+  return rows_range(p->addend, p->rows, p->cols, p->addend_row_stride);
+}
+ByteRange sum_range(const b200_layernorm_params* p) {
+  return rows_range(p->sum, p->rows, p->cols, p->sum_row_stride);
+}
+
+// An output may be an input itself (same base and row stride: each lane reads
+// its columns before it writes them); any other overlap between an output and
+// an input, or between the two outputs, lets warps write rows another warp
+// still reads or writes.
+bool same_rows(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t rows) {
+  return a == b && (rows == 1 || lda == ldb);
+}
+
+// Whether an output aliases an input (the launch then reads x and the addend
+// with coherent loads).  Call only after b200_layernorm_check passed.
+bool aliases(const b200_layernorm_params* p) {
+  const ByteRange y = y_range(p);
+  if (y.overlaps(x_range(p))) return true;
+  if (p->addend && y.overlaps(add_range(p))) return true;
+  if (p->sum) {
+    const ByteRange s = sum_range(p);
+    if (s.overlaps(x_range(p)) || s.overlaps(add_range(p))) return true;
+  }
+  return false;
 }
 
 struct DeviceGuard {
@@ -253,6 +306,23 @@ extern "C" int32_t b200_layernorm_check(const b200_layernorm_params* p) {
         (p->addend_row_stride % 8 != 0 || (p->sum && p->sum_row_stride % 8 != 0)))
       return B200_ATTN_ERR_ALIGNMENT;
   }
+  // outputs: each either disjoint from an input or exactly that input
+  const ByteRange y = y_range(p);
+  if (y.overlaps(x_range(p)) && !same_rows(p->y, p->y_row_stride, p->x, p->x_row_stride, p->rows))
+    return B200_ATTN_ERR_INVALID_ARGUMENT;
+  if (p->addend && y.overlaps(add_range(p)) &&
+      !same_rows(p->y, p->y_row_stride, p->addend, p->addend_row_stride, p->rows))
+    return B200_ATTN_ERR_INVALID_ARGUMENT;
+  if (p->sum) {
+    const ByteRange s = sum_range(p);
+    if (s.overlaps(y)) return B200_ATTN_ERR_INVALID_ARGUMENT;
+    if (s.overlaps(x_range(p)) &&
+        !same_rows(p->sum, p->sum_row_stride, p->x, p->x_row_stride, p->rows))
+      return B200_ATTN_ERR_INVALID_ARGUMENT;
+    if (s.overlaps(add_range(p)) &&
+        !same_rows(p->sum, p->sum_row_stride, p->addend, p->addend_row_stride, p->rows))
+      return B200_ATTN_ERR_INVALID_ARGUMENT;
+  }
   return B200_ATTN_OK;
 }
 
@@ -291,5 +361,7 @@ extern "C" int32_t b200_layernorm_fwd(const b200_layernorm_params* p, void* stre
   a.lda = p->addend ? p->addend_row_stride : 0;
   a.lds = p->sum ? p->sum_row_stride : 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return p->dtype == B200_ATTN_DTYPE_BF16 ? launch<true>(a, s) : launch<false>(a, s);
+  const bool in_place = aliases(p);
+  return p->dtype == B200_ATTN_DTYPE_BF16 ? launch<true>(a, in_place, s)
+                                          : launch<false>(a, in_place, s);
 }

@@ -58,16 +58,18 @@
 #include <mutex>
 
 #include "b200_linear.h"
+#include "byte_range.h"
+#include "error_word.cuh"
 #include "sm100_ptx.cuh"
-
-namespace b200attn {
-// Records the text b200_attn_last_error_detail returns (attn_fwd_sm100.cu).
-void set_error(const char* msg);
-}  // namespace b200attn
 
 namespace b200lin {
 
 namespace ptx = b200attn::ptx;
+using b200attn::ByteRange;
+using b200attn::count_launch;
+using b200attn::rows_range;
+using b200attn::report_error;
+using b200attn::resolve_error_word;
 using b200attn::set_error;
 
 constexpr int kBM = 128;  // output rows per tile = TMEM lanes
@@ -203,7 +205,7 @@ __device__ __noinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity,
     if (*abort_flag) return false;
     if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
       *abort_flag = 1u;
-      if (err) atomicOr(err, B200_ATTN_DEVERR_WAIT_TIMEOUT);
+      report_error(err, B200_ATTN_DEVERR_WAIT_TIMEOUT);
       return false;
     }
   }
@@ -759,6 +761,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t out0 = sbase + C::kOffOut + static_cast<uint32_t>(half * 2 * C::kOutBufBytes);
     static_assert(C::kBlocksPerHalf == 2, "one staging buffer per block of the tile");
     int tc = 0;
+    int armed_tc = -1;  // elected thread: last tile whose residual loads it issued
     for (int t = pair; t < args.num_tiles; t += num_pairs, ++tc) {
       const int buf = tc & 1;
       const uint32_t use = static_cast<uint32_t>(tc >> 1);
@@ -778,6 +781,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ptx::tma_load_2d(out0 + b * C::kOutBufBytes, &tm_r, rb, cbase + b * C::kOutBlockCols,
                              row0);
           }
+          armed_tc = tc;
         }
       }
       bool keep = true;
@@ -837,6 +841,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
+    }
+    if constexpr (kRes) {
+      // After an abort, residual loads of the last tile may still be writing
+      // shared memory: let them land (bounded) before the CTA can exit.  On
+      // the normal path every armed barrier has completed and this returns at
+      // once.
+      if (elected && armed_tc >= 0) {
+#pragma unroll
+        for (int b = 0; b < C::kBlocksPerHalf; ++b) {
+          const uint32_t rb = bar(C::kBarRes + half * 2 + b);
+          const uint64_t t0 = ptx::globaltimer_ns();
+          while (!ptx::mbar_try_wait(rb, static_cast<uint32_t>(armed_tc) & 1u) &&
+                 ptx::globaltimer_ns() - t0 < kWaitTimeoutNs) {
+          }
+        }
+      }
     }
     if (elected) ptx::bulk_wait_group_all();  // stores complete before the CTA ends
   }
@@ -947,6 +967,7 @@ int launch(const CUtensorMap& mx, const CUtensorMap& mw, const LinArgs& a, int d
     set_error(cudaGetErrorString(e));
     return B200_ATTN_ERR_LAUNCH;
   }
+  count_launch();
   return B200_ATTN_OK;
 }
 
@@ -983,6 +1004,7 @@ int launch_pair(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap&
     set_error(cudaGetErrorString(e));
     return B200_ATTN_ERR_LAUNCH;
   }
+  count_launch();
   return B200_ATTN_OK;
 }
 
@@ -1056,6 +1078,17 @@ extern "C" int32_t b200_linear_check(const b200_linear_params* p) {
     return B200_ATTN_ERR_ALIGNMENT;
   if (p->n > 1 && p->w_row_stride % 8 != 0) return B200_ATTN_ERR_ALIGNMENT;
   if (p->residual && p->m > 1 && p->residual_row_stride % 8 != 0) return B200_ATTN_ERR_ALIGNMENT;
+  // y must not overlap any input: its stores would race the TMA loads of x,
+  // W and the residual prefetch
+  const ByteRange yr = rows_range(p->y, p->m, p->n, p->y_row_stride);
+  if (yr.overlaps(rows_range(p->x, p->m, p->k, p->x_row_stride)) ||
+      yr.overlaps(rows_range(p->w, p->n, p->k, p->w_row_stride)) ||
+      (p->bias && yr.overlaps(rows_range(p->bias, 1, p->n, p->n))) ||
+      (p->residual && yr.overlaps(rows_range(p->residual, p->m, p->n, p->residual_row_stride))) ||
+      (p->row_mask && yr.overlaps(ByteRange{reinterpret_cast<uintptr_t>(p->row_mask),
+                                            reinterpret_cast<uintptr_t>(p->row_mask) +
+                                                static_cast<uintptr_t>(p->m)})))
+    return B200_ATTN_ERR_INVALID_ARGUMENT;
   return B200_ATTN_OK;
 }
 
@@ -1124,7 +1157,7 @@ extern "C" int32_t b200_linear_fwd(const b200_linear_params* p, void* stream) {
   a.masked_keep_residual = p->masked_rows == B200_LINEAR_MASKED_KEEP_RESIDUAL ? 1 : 0;
   a.y = static_cast<uint16_t*>(p->y);
   a.ld_y = p->y_row_stride;
-  a.err = p->error_word;
+  if ((rc = resolve_error_word(p->error_word, &a.err)) != B200_ATTN_OK) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (pair) {
     // the output (and the residual) leave and enter through 64 x 128 TMA boxes

@@ -63,7 +63,11 @@ def test_params_struct_layout_matches_c(tmp_path):
 
 
 def test_abi_version(lib):
-    assert lib.b200_attn_abi_version() == 1
+    assert lib.b200_attn_abi_version() == 2
+
+
+def test_launch_counter_starts_without_gpu_work(lib):
+    assert lib.b200_attn_launch_count() >= 0
 
 
 def test_query_agrees_with_planner_envelope(lib):
@@ -74,6 +78,27 @@ def test_query_agrees_with_planner_envelope(lib):
             supported = 1 if dtype in (0, 1) and d in SM100_HEAD_DIMS else 0
             assert lib.b200_attn_query(dtype, d, 1, 0) == supported
     assert set(SM100_HEAD_DIMS) == set(range(8, 129, 8))
+
+
+def test_launch_shape_agrees_with_planner(lib):
+    """The planner's launch metadata and the kernel's own launch shape come
+    from one definition: b200_attn_launch_shape reports what b200_attn_fwd
+    launches, and the planner's constants must equal it."""
+    from b200_attention.attention_dispatch import (SM100_BLOCK_M, SM100_BLOCK_N, SM100_NUM_WARPS,
+                                                   _sm100_launch)
+
+    for dtype in (_native.DTYPE_BF16, _native.DTYPE_FP16):
+        for d in SM100_HEAD_DIMS:
+            shape = _native.launch_shape(dtype, d)
+            assert shape is not None, (dtype, d)
+            launch = _sm100_launch(d)
+            assert (shape["block_m"], shape["block_n"], shape["num_warps"], shape["ring_slots"]) == (
+                launch.block_m, launch.block_n, launch.num_warps, launch.num_stages), (dtype, d)
+            assert (shape["block_m"], shape["block_n"], shape["num_warps"]) == (
+                SM100_BLOCK_M, SM100_BLOCK_N, SM100_NUM_WARPS)
+            assert shape["rows_per_cta"] == 2 * shape["block_m"]
+    assert _native.launch_shape(_native.DTYPE_BF16, 136) is None
+    assert _native.launch_shape(9, 64) is None
 
 
 def _params(**kw):
@@ -132,7 +157,7 @@ def test_check_rejects_unaligned_stride(lib):
 
 
 def test_error_strings(lib):
-    for code in range(7):
+    for code in range(8):
         assert lib.b200_attn_error_string(code)
     assert b"unknown" in lib.b200_attn_error_string(99)
 

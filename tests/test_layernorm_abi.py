@@ -49,7 +49,8 @@ def test_params_struct_layout_matches_c(tmp_path):
 
 def _params(**kw):
     p = _native.LayerNormParams()
-    p.x, p.y, p.weight, p.bias = 0x100000, 0x200000, 0x300000, 0x300800
+    # operands 256 MB apart: no two ranges overlap unless a case says so
+    p.x, p.y, p.weight, p.bias = 0x10000000, 0x20000000, 0x30000000, 0x30000800
     p.rows, p.cols, p.x_row_stride, p.y_row_stride = 16384, 1024, 1024, 1024
     p.eps, p.dtype = 1e-5, _native.DTYPE_BF16
     for k, v in kw.items():
@@ -70,15 +71,26 @@ def _params(**kw):
     (dict(cols=8192, x_row_stride=8192, y_row_stride=8192), _native.ERR_UNSUPPORTED),
     (dict(cols=1020, x_row_stride=1024, y_row_stride=1024), _native.ERR_ALIGNMENT),
     (dict(x_row_stride=1000), _native.ERR_INVALID_ARGUMENT),
-    (dict(y=0x200004), _native.ERR_ALIGNMENT),
-    (dict(bias=0x300802), _native.ERR_ALIGNMENT),
-    (dict(addend=0x400000, addend_row_stride=1024), _native.OK),
-    (dict(addend=0x400000, addend_row_stride=1024, sum=0x100000, sum_row_stride=1024), _native.OK),
-    (dict(sum=0x500000, sum_row_stride=1024), _native.ERR_INVALID_ARGUMENT),  # sum without addend
-    (dict(addend=0x400000, addend_row_stride=1024, sum=0x200000, sum_row_stride=1024),
+    (dict(y=0x20000004), _native.ERR_ALIGNMENT),
+    (dict(bias=0x30000802), _native.ERR_ALIGNMENT),
+    (dict(addend=0x40000000, addend_row_stride=1024), _native.OK),
+    (dict(addend=0x40000000, addend_row_stride=1024, sum=0x10000000, sum_row_stride=1024),
+     _native.OK),  # the sum written over x in place
+    (dict(sum=0x50000000, sum_row_stride=1024), _native.ERR_INVALID_ARGUMENT),  # sum without addend
+    (dict(addend=0x40000000, addend_row_stride=1024, sum=0x20000000, sum_row_stride=1024),
      _native.ERR_INVALID_ARGUMENT),  # sum onto the normalised output
-    (dict(addend=0x400000, addend_row_stride=1000), _native.ERR_INVALID_ARGUMENT),
-    (dict(addend=0x400008, addend_row_stride=1024), _native.ERR_ALIGNMENT),
+    (dict(addend=0x40000000, addend_row_stride=1000), _native.ERR_INVALID_ARGUMENT),
+    (dict(addend=0x40000008, addend_row_stride=1024), _native.ERR_ALIGNMENT),
+    # in place (an output that IS an input) is allowed; any other overlap is not
+    (dict(y=0x10000000), _native.OK),
+    (dict(y=0x10000010), _native.ERR_INVALID_ARGUMENT),  # y shifted over x by 8 elements
+    (dict(y=0x10000000, y_row_stride=2048), _native.ERR_INVALID_ARGUMENT),  # same base, other stride
+    (dict(y=0x0ffff000), _native.ERR_INVALID_ARGUMENT),  # y's last rows over x's first
+    (dict(addend=0x40000000, addend_row_stride=1024, y=0x40000000), _native.OK),
+    (dict(addend=0x40000000, addend_row_stride=1024, sum=0x40000800, sum_row_stride=1024),
+     _native.ERR_INVALID_ARGUMENT),  # sum shifted over the addend
+    (dict(addend=0x40000000, addend_row_stride=1024, sum=0x1fffff00, sum_row_stride=1024),
+     _native.ERR_INVALID_ARGUMENT),  # sum's last row over y's first
 ])
 def test_check(lib, kw, code):
     assert lib.b200_layernorm_check(ctypes.byref(_params(**kw))) == code

@@ -63,9 +63,9 @@ def test_params_struct_layout_matches_c(tmp_path):
 
 def _params(**kw):
     p = _native.LinearParams()
-    base = 0x100000
-    p.x, p.w, p.y = base, base + 0x1000000, base + 0x2000000
-    p.bias = base + 0x3000000
+    # operands 256 MB apart: no two ranges overlap
+    p.x, p.w, p.y = 0x10000000, 0x20000000, 0x30000000
+    p.bias = 0x40000000
     p.m, p.n, p.k = 16384, 4096, 1024
     p.x_row_stride, p.w_row_stride, p.y_row_stride = 1024, 1024, 4096
     p.dtype = _native.DTYPE_BF16
@@ -81,7 +81,7 @@ def _check(lib, p):
 def test_check_accepts_valid_params(lib):
     assert _check(lib, _params()) == _native.OK
     assert _check(lib, _params(activation=_native.LINEAR_ACT_GELU)) == _native.OK
-    res = 0x100000 + 0x4000000
+    res = 0x50000000
     assert _check(lib, _params(residual=res, residual_row_stride=4096, row_mask=0x7000,
                                masked_rows=_native.LINEAR_MASKED_KEEP_RESIDUAL)) == _native.OK
     assert _check(lib, _params(m=1, x_row_stride=3)) == _native.OK  # row stride unused for one row
@@ -102,9 +102,16 @@ def test_check_accepts_valid_params(lib):
     (dict(x_row_stride=1000), _native.ERR_INVALID_ARGUMENT),  # shorter than K
     (dict(n=4100, y_row_stride=4100, k=1024), _native.ERR_ALIGNMENT),  # N not a multiple of 8
     (dict(k=1020, x_row_stride=1024, w_row_stride=1024), _native.ERR_ALIGNMENT),
-    (dict(x=0x100008), _native.ERR_ALIGNMENT),
-    (dict(bias=0x3000002), _native.ERR_ALIGNMENT),
+    (dict(x=0x10000008), _native.ERR_ALIGNMENT),
+    (dict(bias=0x40000002), _native.ERR_ALIGNMENT),
     (dict(y_row_stride=4100), _native.ERR_ALIGNMENT),
+    # y overlapping an input: its stores would race the input's loads
+    (dict(y=0x10000000), _native.ERR_INVALID_ARGUMENT),  # y == x
+    (dict(y=0x1ffff000), _native.ERR_INVALID_ARGUMENT),  # y's first rows over W
+    (dict(bias=0x30000100), _native.ERR_INVALID_ARGUMENT),
+    (dict(residual=0x30000000, residual_row_stride=4096), _native.ERR_INVALID_ARGUMENT),
+    (dict(residual=0x2ffff000, residual_row_stride=4096), _native.ERR_INVALID_ARGUMENT),
+    (dict(row_mask=0x30000010), _native.ERR_INVALID_ARGUMENT),
 ])
 def test_check_rejects(lib, kw, code):
     assert _check(lib, _params(**kw)) == code

@@ -74,13 +74,13 @@ def test_functional_op_rejects_cpu_inputs_loudly():
 def test_error_word_survives_inference_mode(monkeypatch):
     """The per-device error word is created as a normal tensor even when the
     first kernel call happens under torch.inference_mode(), so it can be
-    cleared outside it (CPU stand-in for the CUDA device)."""
+    cleared outside it (unpinned CPU memory stands in for the pinned word)."""
     from b200_attention import fused_attention as fa
 
     real_zeros = torch.zeros
 
     def fake_zeros(*args, **kwargs):
-        kwargs["device"] = "cpu"
+        assert kwargs.pop("pin_memory", False), "the error word lives in pinned host memory"
         return real_zeros(*args, **kwargs)
 
     monkeypatch.setattr(fa, "_error_words", {})

@@ -96,7 +96,8 @@ def test_e2e_config_plans_every_layer_on_sm100():
     spec = AttentionModelSpec(8, 2048, 1024, 16, 4096, 12, True)
     plan = select_attention_stack_plan(spec, _rt(d=1024))
     assert len(plan.layers) == 12 and {p.mode for p in plan.layers} == {AttentionMode.SM100_FUSED}
-    assert plan.layers[0].launch.num_stages == 3
+    launch = plan.layers[0].launch
+    assert (launch.block_m, launch.block_n, launch.num_warps, launch.num_stages) == (128, 128, 11, 10)
 
 
 def test_cache_and_invalid_specs():
