@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark of the sm_100a fused attention forward (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg4]
     python bench.py --impl reference ...      # reference's CPU attention path
     python bench.py --impl torch-dense ...    # yardstick: the reference's dense path on this GPU
 
@@ -40,7 +40,9 @@ UNIT = "TFLOP/s"
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# BASELINE configs (configs[1] is the default workload; "ns" is the north-star shape).
+# BASELINE configs.  The default workload is configs[3] (cfg4), the largest
+# configuration that fits one GPU at N = 1 (all 32 heads; 4 heads per GPU at
+# N = 8); "ns" is the north-star shape.
 WORKLOADS = {
     "cfg1": dict(B=2, H=8, S=512, D=64, causal=True, masked=False, shard="batch"),
     "cfg2": dict(B=8, H=16, S=2048, D=128, causal=True, masked=False, shard="batch"),
@@ -73,6 +75,54 @@ def load_peaks() -> tuple[dict, str]:
     if path.exists():
         return json.loads(path.read_text()), "measured"
     return dict(FALLBACK_PEAKS), "fallback"
+
+
+def algorithmic_bytes(cfg: dict, batch: int, heads: int, lengths: list[int] | None) -> float:
+    """Minimum HBM bytes of one launch: Q, K and V read once and O written once
+    (for key-padded batches only the valid query and key rows are read, the
+    whole output is written), plus the key mask."""
+    S, D = cfg["S"], cfg["D"]
+    elem = 4 if cfg.get("dtype") == "float32" else 2
+    if lengths is not None:
+        rows_read = heads * 3 * sum(lengths)
+        return float(elem * D * (rows_read + batch * heads * S) + batch * S)
+    return float(4 * batch * heads * S * D * elem)
+
+
+def roofline(flop: float, nbytes: float, launch_ms: float, peaks: dict, peak_src: str,
+             traffic, traffic_source) -> dict:
+    """Roofline of one launch.  The bound is the roof the arithmetic intensity
+    puts the kernel under: tensor when FLOP/byte is above the ridge (measured
+    bf16 peak / measured HBM bandwidth), HBM otherwise; both fractions are
+    reported."""
+    tflops = flop / (launch_ms * 1e-3) / 1e12
+    gbs = nbytes / (launch_ms * 1e-3) / 1e9
+    ai = flop / nbytes
+    ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    tensor = {"achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+              "frac": tflops / peaks["bf16_tflops"]}
+    hbm = {"achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"]}
+    main = tensor if ai >= ridge else hbm
+    return {
+        "bound": "tensor" if ai >= ridge else "hbm", **main, "traffic": traffic,
+        "algorithmic_bytes": nbytes, "flop": flop, "arithmetic_intensity": ai, "ridge": ridge,
+        "tensor": tensor, "hbm": hbm, "avg_launch_ms": launch_ms,
+        "peak_source": f"{peak_src} bf16_tflops (burst, kernel timed alone) and hbm_gbs",
+        "traffic_source": traffic_source,
+    }
+
+
+def stored_traffic(name: str, scale: float = 1.0):
+    """DRAM bytes per launch from a committed ncu capture (profiles/), scaled
+    to this rank's share of the launch, with the capture's provenance."""
+    prof = ROOT / "profiles" / name
+    if not prof.exists():
+        return None, None
+    data = json.loads(prof.read_text())
+    traffic = data.get("dram_bytes_per_launch")
+    source = {"file": f"profiles/{name}", "commit": data.get("captured_at_commit"),
+              "workload": data.get("workload")}
+    return (traffic * scale if traffic is not None else None), source
 
 
 def valid_lengths(cfg: dict, seed: int) -> list[int] | None:
@@ -223,14 +273,21 @@ class CpuReference:
             self.ora.reference_attention(self.q, self.k, self.v, self.mask, self.causal, self.D ** -0.5)
         return time.perf_counter() - t0
 
-    def measure(self, budget_s: float, min_reps: int = 1) -> dict:
+    def measure(self, budget_s: float, min_reps: int = 1, full_flop: float | None = None) -> dict:
         times = []
         while sum(times) < budget_s or len(times) < min_reps:
             times.append(self.call())
         med = statistics.median(times)
-        return {"value": self.flop / med / 1e12, "unit": UNIT,
-                "cores": self.torch.get_num_threads(), "kind": "port",
-                "ms_per_sample": med * 1e3, "sample": f"{len(times)} reps of " + self.desc}
+        rate = self.flop / med
+        out = {"value": rate / 1e12, "unit": UNIT,
+               "cores": self.torch.get_num_threads(), "kind": "port",
+               "ms_per_sample": med * 1e3, "sample": f"{len(times)} reps of " + self.desc}
+        if full_flop:
+            # the metric's "vs CPU ms": the whole step on the CPU at the sampled rate
+            out["ms_per_step_extrapolated"] = full_flop / rate * 1e3
+            out["sample"] += (f"; full step extrapolated at the sampled FLOP rate: "
+                              f"{full_flop / 1e12:.3f} TFLOP / {rate / 1e12:.3f} TFLOP/s")
+        return out
 
 
 def run_reference_arm(args, cfg: dict, rank: int, world: int) -> int:
@@ -243,6 +300,8 @@ def run_reference_arm(args, cfg: dict, rank: int, world: int) -> int:
     times = [ref.call() for _ in range(args.steps)]
     ms = statistics.median(times) * 1e3
     value = ref.flop / (ms * 1e-3) / 1e12
+    B, H, _ = shard_for(cfg, 1, 0)
+    full_flop = flops_for(cfg, B, H, valid_lengths(cfg, args.seed))
     line = {
         "impl": "reference",
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -252,7 +311,9 @@ def run_reference_arm(args, cfg: dict, rank: int, world: int) -> int:
         "config": {"workload": args.workload, **{k: cfg[k] for k in ("B", "H", "S", "D", "causal")},
                    "impl_path": "oracle.reference_attention on host CPU cores"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": ref.torch.get_num_threads(),
-                         "kind": "port", "sample": f"{args.steps} timed reps of " + ref.desc},
+                         "kind": "port", "sample": f"{args.steps} timed reps of " + ref.desc
+                         + f"; full step extrapolated at the sampled FLOP rate",
+                         "ms_per_step_extrapolated": full_flop / (value * 1e12) * 1e3},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -345,6 +406,7 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
     import torch
     import torch.distributed as dist
 
+    from b200_attention import _native
     from b200_attention.fused_attention import b200_fused_attention, read_device_errors
     from b200_attention.transformer import Decoder, DecoderConfig, init_normal_
 
@@ -383,8 +445,10 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
             with torch.cuda.stream(cap):
                 model(static_tokens)
                 cap.synchronize()
+                c0 = _native.launch_count()
                 with torch.cuda.graph(graph, stream=cap):
                     static_out = model(static_tokens)
+                graph_launches = _native.launch_count() - c0
             stream.wait_stream(cap)
 
             def forward(tok):
@@ -394,6 +458,7 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
         sampler = ClockSampler(local_rank)
         barrier()
         torch.cuda.synchronize(dev)
+        launches0 = _native.launch_count()
         with sampler:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
@@ -402,6 +467,10 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
             e1.record(stream)
             torch.cuda.synchronize(dev)
         barrier()
+        # this package's kernel launches inside the timed region (a graph's
+        # launches were counted once, at capture, and replay once per step)
+        launches = (graph_launches * args.steps if graph is not None
+                    else _native.launch_count() - launches0)
         ms_per_step = max_over_ranks(e0.elapsed_time(e1)) / args.steps
         value = flop_job / (ms_per_step * 1e-3) / 1e12
         finite = bool(torch.isfinite(out.float()).all())
@@ -467,12 +536,14 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = CpuReference(cfg, args.seed).measure(args.cpu_budget, min_reps=3)
+        cpu["sample"] += " (the decoder's attention core; no CPU decoder is timed)"
     peaks, peak_src = load_peaks()
-    peak = peaks["bf16_tflops"]
-    traffic = None
-    prof = ROOT / "profiles" / "attn_fwd_sm100_cfg5_traffic.json"
-    if prof.exists() and world == 1:  # captured at the N = 1 per-layer shape
-        traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
+    traffic, traffic_src = None, None
+    if world == 1:  # captured at the N = 1 per-layer shape
+        traffic, traffic_src = stored_traffic("attn_fwd_sm100_cfg5_traffic.json")
+    roof = roofline(attn_flop, algorithmic_bytes(cfg, B, H, None), attn_ms, peaks, peak_src,
+                    traffic, traffic_src)
+    roof["kernel"] = "attn_fwd_sm100_kernel at the per-rank attention shape of one layer"
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -497,18 +568,13 @@ def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, 
                    "flop_per_step_job": flop_job},
         "attention": {"tflops": attn_tflops, "ms_per_layer": attn_ms,
                       "share_of_forward": cfg["layers"] * attn_ms / ms_per_step},
-        "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": peak, "unit": "TFLOP/s",
-                     "frac": attn_tflops / peak, "traffic": traffic,
-                     "kernel": "attn_fwd_sm100_kernel at the per-rank attention shape",
-                     "peak_source": f"{peak_src} bf16_tflops (burst, kernel timed alone)"},
+        "roofline": roof,
         "cpu_baseline": cpu,
         "e2e": {"value": flop_rank / (e2e_ms * 1e-3) / 1e12 * world, "unit": "TFLOP/s (decoder forward)",
                 "h2d_bytes_per_step": htoks[0].numel() * htoks[0].element_size(),
                 "d2h_bytes_per_step": hout.numel() * hout.element_size(), "ms_per_step": e2e_ms,
                 "pipelining": "step i+1's forward overlaps step i's download (copy stream)"},
-        # per layer: the attention kernel, plus (fused) out_proj and ffn_in on the
-        # fused linear kernel and norm1/norm2 on the LayerNorm kernel; and the final norm
-        "gpu_launches": args.steps * (cfg["layers"] * 5 + 1 if fused else cfg["layers"]),
+        "gpu_launches": launches,
         "clocks": sampler.summary(),
         "validation": {"finite": finite, "device_errors": errors, "e2e_bit_exact": e2e_exact},
     }
@@ -521,7 +587,7 @@ def main(argv=None) -> int:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="cfg4", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "torch-dense"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work")
@@ -550,8 +616,7 @@ def main(argv=None) -> int:
     import torch.distributed as dist
 
     from b200_attention import _native
-    from b200_attention.fused_attention import (b200_fused_attention, device_error_word,
-                                                read_device_errors)
+    from b200_attention.fused_attention import b200_fused_attention, read_device_errors
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -631,15 +696,18 @@ def main(argv=None) -> int:
         with torch.cuda.stream(cap):
             step(0)
             cap.synchronize()
+            c0 = _native.launch_count()
             with torch.cuda.graph(graph, stream=cap):
                 for i in range(args.steps):
                     step(i)
+            graph_launches = _native.launch_count() - c0
         stream.wait_stream(cap)
         graph.replay()
         torch.cuda.synchronize(dev)
     sampler = ClockSampler(local_rank)
     barrier()
     torch.cuda.synchronize(dev)
+    launches0 = _native.launch_count()
     with sampler:
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
@@ -654,6 +722,9 @@ def main(argv=None) -> int:
         t_end.record(stream)
         torch.cuda.synchronize(dev)
     barrier()
+    # launches the library issued inside the timed region (a graph's launches
+    # were counted once, at capture)
+    launches = graph_launches if graph is not None else _native.launch_count() - launches0
     elapsed_ms = max_over_ranks(t_start.elapsed_time(t_end))
     if graph is not None:
         avg_launch_ms = t_start.elapsed_time(t_end) / args.steps  # back-to-back launches
@@ -662,7 +733,6 @@ def main(argv=None) -> int:
     errors = read_device_errors(dev)
     ms_per_step = elapsed_ms / args.steps
     value = flop_job / (ms_per_step * 1e-3) / 1e12
-    achieved = flop_rank / (avg_launch_ms * 1e-3) / 1e12  # this rank's kernel, per launch
 
     # ---- validation gather (outside the timed region): finiteness and a checksum per rank
     o = outs[(args.steps - 1) % n_sets].float()
@@ -740,20 +810,16 @@ def main(argv=None) -> int:
     # ---- CPU baseline (rank 0, N = 1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = CpuReference(cfg, args.seed).measure(args.cpu_budget, min_reps=3)
+        cpu = CpuReference(cfg, args.seed).measure(args.cpu_budget, min_reps=3, full_flop=flop_job)
 
     peaks, peak_src = load_peaks()
     peak = peaks["bf16_tflops"]
-    traffic = None
-    prof = ROOT / "profiles" / f"attn_fwd_sm100_{args.workload}_traffic.json"
-    if prof.exists():
-        # captured for the whole N = 1 launch; a head-sharded rank processes
-        # H / cfg["H"] of the heads, and the traffic scales with them
-        traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
-        if traffic is not None:
-            traffic = traffic * H / cfg["H"]
-    lib = _native.load_library()
-    launches = args.steps  # one kernel launch per step (b200_attn_launches_per_call == 1)
+    # captured for the whole N = 1 launch; a head-sharded rank processes
+    # H / cfg["H"] of the heads, and the traffic scales with them
+    traffic, traffic_src = stored_traffic(f"attn_fwd_sm100_{args.workload}_traffic.json",
+                                          H / cfg["H"])
+    roof = roofline(flop_rank, algorithmic_bytes(cfg, B, H, lengths), avg_launch_ms, peaks,
+                    peak_src, traffic, traffic_src)
 
     vs_baseline = None
     if "published_ms" in cfg:
@@ -791,12 +857,7 @@ def main(argv=None) -> int:
                if "published_ms" in cfg else {}),
         },
         "pct_of_bf16_peak": 100.0 * value / (peak * world),
-        "roofline": {
-            "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-            "frac": achieved / peak, "traffic": traffic,
-            "peak_source": f"{peak_src} bf16_tflops (burst, kernel timed alone)",
-            "avg_launch_ms": avg_launch_ms,
-        },
+        "roofline": roof,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_ms,
@@ -808,7 +869,6 @@ def main(argv=None) -> int:
     if cpu:
         line["speedup_vs_cpu_e2e"] = e2e_value / cpu["value"]
     print(json.dumps(line), flush=True)
-    _ = lib, device_error_word
     return 0
 
 

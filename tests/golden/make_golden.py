@@ -12,6 +12,12 @@ Writes, next to this script:
 * ``planner_plans.json`` — the reference planner's plans
   (model/attention_dispatch.py:563) for the reference's 14 published shapes
   (tools/benchmark_shape_matrix.py) x dtype x device capability.
+* ``model_cases.json`` + ``model_cases.npz`` — the reference's own
+  ``BaselineTransformer`` (torch_transformer_benchmark.py:126-171) on CPU, with
+  weights from ``tests_golden_io.seeded_state_dict`` and hidden states from the
+  reference harness's ``generate_random_case`` (:362-400): for every block
+  (fed the previous block's reference output) its attention sublayer's output
+  and its own output, and the output of the whole model.
 
 The reference is imported read-only; nothing of it is copied.  The fixtures are
 what the reference computed, which is what the oracle must reproduce.
@@ -48,6 +54,59 @@ KEEP_HEADS = {"cfg1_bf16_causal_heads01": 2}
 
 DTYPES = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}
 
+# Model cases: a 2-layer pre-LN decoder with the end-to-end configuration's
+# head size (d_model 128, 2 heads of 64, FFN 512), B 2 x S 64.
+# (name, dtype, causal, padding_ratio, seed); padding_ratio 0 gives the
+# harness's all-ones mask, None no mask at all.
+MODEL_SHAPE = dict(batch=2, seq_len=64, d_model=128, num_heads=2, ffn_dim=512, num_layers=2)
+MODEL_WEIGHT_SEED = 4321
+MODEL_CASES = [
+    ("fp32_causal", "float32", True, 0.0, 1234),
+    ("bf16_causal_nomask", "bfloat16", True, None, 1236),
+    ("bf16_full_padded", "bfloat16", False, 0.5, 1237),
+    ("fp16_causal_padded", "float16", True, 0.25, 1238),
+]
+
+
+def make_model_cases(reference_module):
+    """Per-block and whole-model outputs of the reference's BaselineTransformer."""
+    from tests_golden_io import model_digest, seeded_state_dict
+
+    tb = reference_module
+    meta, arrays = [], {}
+    for name, dtype_name, causal, padding, seed in MODEL_CASES:
+        dtype = DTYPES[dtype_name]
+        cfg = tb.TransformerConfig(MODEL_SHAPE["batch"], MODEL_SHAPE["seq_len"],
+                                   MODEL_SHAPE["d_model"], MODEL_SHAPE["num_heads"],
+                                   MODEL_SHAPE["ffn_dim"], MODEL_SHAPE["num_layers"], causal)
+        model = tb.BaselineTransformer(cfg)
+        model.load_state_dict(seeded_state_dict(model.state_dict(), MODEL_WEIGHT_SEED, dtype))
+        model = model.to(dtype).eval()
+        x, mask = tb.generate_random_case(cfg, torch.device("cpu"), dtype, seed,
+                                          0.0 if padding is None else padding, 1.0)
+        if padding is None:
+            mask = None
+        with torch.inference_mode():
+            h = x
+            for i, layer in enumerate(model.layers):
+                # the attention sublayer alone (the part the attention kernel
+                # computes, with its projections), then the whole block
+                arrays[f"{name}.attn{i}"] = to_bits(layer.attention(layer.norm1(h), mask, causal))
+                h = layer(h, mask, causal)
+                arrays[f"{name}.block{i}"] = to_bits(h)
+            arrays[f"{name}.out"] = to_bits(model(x, mask))
+        meta.append({"name": name, "dtype": dtype_name, "causal": causal, "padding_ratio": padding,
+                     "seed": seed, **MODEL_SHAPE, "weight_seed": MODEL_WEIGHT_SEED,
+                     "lengths": None if mask is None else mask.sum(1).tolist(),
+                     "input_sha256": model_digest(x, mask)})
+    np.savez_compressed(HERE / "model_cases.npz", **arrays)
+    (HERE / "model_cases.json").write_text(json.dumps(
+        {"torch": torch.__version__,
+         "source": "reference BaselineTransformer (torch_transformer_benchmark.py) on CPU; "
+                   "inputs from its generate_random_case",
+         "cases": meta}, indent=1) + "\n")
+    return len(meta)
+
 
 def make_inputs(shape, dtype_name, lengths, seed):
     """Q, K, V ~ N(0,1) fp32 from a seeded CPU generator, cast (reference
@@ -82,6 +141,8 @@ def main() -> None:
     ap.add_argument("--reference", required=True, help="checkout of the reference repository")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
+    sys.path.insert(0, str(HERE.parent))  # tests/ (tests_golden_io)
+    import torch_transformer_benchmark
     from model.attention_dispatch import AttentionModelSpec, AttentionRuntime, select_attention_stack_plan
     from model.triton_fused_attention import triton_fused_attention
     from tools.benchmark_shape_matrix import ANNOUNCED_CASES
@@ -128,7 +189,8 @@ def main() -> None:
                                    for p in sp.layers],
                     })
     (HERE / "planner_plans.json").write_text(json.dumps(plans, indent=0) + "\n")
-    print(f"wrote {len(meta)} attention cases and {len(plans)} plans")
+    n_models = make_model_cases(torch_transformer_benchmark)
+    print(f"wrote {len(meta)} attention cases, {len(plans)} plans and {n_models} model cases")
 
 
 if __name__ == "__main__":

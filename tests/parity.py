@@ -53,3 +53,40 @@ def assert_close(out: torch.Tensor, ref: torch.Tensor, label: str = "") -> dict:
     assert r["max_abs"] <= MAX_ABS, f"{label}: max-abs {r}"
     assert r["mean_abs"] <= MEAN_ABS, f"{label}: mean-abs {r}"
     return r
+
+
+def unit_in_last_place(ref: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Unit in the last place of each element of ``ref`` in ``dtype``."""
+    mant = {torch.bfloat16: 7, torch.float16: 10, torch.float32: 23}[dtype]
+    mag = ref.float().abs().clamp_min(torch.finfo(dtype).tiny)
+    return torch.exp2(torch.floor(torch.log2(mag)) - mant)
+
+
+# A block's output is a 16-bit residual stream, rounded three times after the
+# attention sublayer: x1 = round(x + attention), f = ffn(LayerNorm(x1)) rounded
+# at each of its steps, out = round(x1 + f).  Two implementations whose
+# attention differs in its last bits can differ by one unit of the stream's
+# magnitude in x1, by up to two units where that flip passes through the
+# LayerNorm and the FFN into f, and by one more in the final sum: four units in
+# the last place of the row's largest magnitude.  (The reference block with an
+# exact fp32 attention core reaches 1.5 units against the bf16 block at the
+# end-to-end configuration, whose stream grows to |x| ~ 9, where one bf16 unit
+# is 0.0625 -- above the 2e-2 of an attention output of magnitude < 2.)  The
+# bound for a block's output is max(MAX_ABS, BLOCK_UNITS such units) per
+# element, with the mean-abs bound unchanged.
+BLOCK_UNITS = 4
+
+
+def assert_block_close(out: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype,
+                       label: str = "") -> dict:
+    """A decoder block's output against the reference block's: the mean-abs
+    bound, the NaN pattern, and max(MAX_ABS, BLOCK_UNITS row units) per element."""
+    r = compare(out, ref)
+    assert r["same_nan"], f"{label}: NaN pattern differs {r}"
+    assert r["mean_abs"] <= MEAN_ABS, f"{label}: mean-abs {r}"
+    o, f = out.float().cpu(), ref.float().cpu()
+    row_max = f.abs().nan_to_num(0.0).amax(dim=-1, keepdim=True)
+    bound = torch.clamp(BLOCK_UNITS * unit_in_last_place(row_max, dtype), min=MAX_ABS)
+    d = (o - f).abs().nan_to_num(0.0)
+    assert bool((d <= bound).all()), f"{label}: worst {float((d - bound).max()):.3e} over the bound {r}"
+    return r

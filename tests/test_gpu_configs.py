@@ -52,20 +52,20 @@ def test_cfg2_full():
         assert_close(out[b:b + 1], ref, f"cfg2 batch {b}")
 
 
-def test_cfg3_key_padded_sampled():
+def test_cfg3_key_padded_every_batch_entry():
     B, H, S, D = 16, 32, 4096, 128
     q, k, v = seeded_qkv((B, H, S, D), torch.bfloat16, 1234)
     gen = torch.Generator("cpu").manual_seed(1234 + 7)
     lengths = torch.randint(S // 4, S + 1, (B,), generator=gen)
     mask = torch.arange(S)[None, :] < lengths[:, None]
     out = _kernel(q, k, v, mask, False, zero_q=True)
-    order = torch.argsort(lengths)
-    for b in (int(order[0]), int(order[B // 2]), int(order[-1])):
-        for h in (0, H - 1):
-            sl = (slice(b, b + 1), slice(h, h + 1))
-            ref = reference_attention(q[sl], k[sl], v[sl], mask[b:b + 1], False, D ** -0.5)
-            ref = zero_masked_rows(ref, mask[b:b + 1])
-            assert_close(out[sl], ref, f"cfg3 b={b} L={int(lengths[b])} h={h}")
+    # one head of every batch entry (every valid length), heads spread over 0..H-1
+    for b in range(B):
+        h = (b * 7) % H
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        ref = reference_attention(q[sl], k[sl], v[sl], mask[b:b + 1], False, D ** -0.5)
+        ref = zero_masked_rows(ref, mask[b:b + 1])
+        assert_close(out[sl], ref, f"cfg3 b={b} L={int(lengths[b])} h={h}")
 
 
 @pytest.mark.parametrize("name,shape", [("ns", (8, 16, 8192, 128)), ("cfg4", (1, 32, 32768, 128)),

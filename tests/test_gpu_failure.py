@@ -56,3 +56,44 @@ def test_selftest_rejects_configurations_it_does_not_cover():
                          device_error_word(dev))
     lib = _native.load_library()
     assert lib.b200_attn_selftest_stall(ctypes.byref(params), 0, None) == _native.ERR_UNSUPPORTED
+
+
+def test_module_and_decoder_raise_after_a_device_reported_timeout():
+    """After a launch reports a pipeline timeout in the device's error word,
+    the operator, the module and the decoder raise DeviceError instead of
+    returning a tensor (the C ABI refuses to launch while the host-visible word
+    holds the report); clearing the word resumes normal, correct launches."""
+    from b200_attention import DeviceError, check_device_errors, clear_device_errors
+    from b200_attention.modules import B200FusedSelfAttention
+    from b200_attention.transformer import Decoder, DecoderConfig, init_normal_
+
+    dev = torch.device("cuda", 0)
+    clear_device_errors(dev)
+    q, k, v = (t.to(dev) for t in seeded_qkv((1, 2, 512, 128), torch.bfloat16, 37))
+    params = make_params(q, k, v, torch.empty_like(q), None, True, 128 ** -0.5, False,
+                         device_error_word(dev))
+    lib = _native.load_library()
+    rc = lib.b200_attn_selftest_stall(ctypes.byref(params), 1,
+                                      ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+    assert rc == _native.OK
+    torch.cuda.synchronize(dev)  # the stalled launch has finished and reported
+
+    module = B200FusedSelfAttention(256, 4).to(dev, torch.bfloat16).eval()
+    decoder = init_normal_(Decoder(DecoderConfig(2, 128, 256, 4, 512, 2, True)), seed=3)
+    decoder = decoder.to(dev, torch.bfloat16).eval()
+    x = torch.randn(2, 128, 256, device=dev, dtype=torch.bfloat16)
+    with torch.inference_mode():
+        with pytest.raises(DeviceError, match="timeout"):
+            check_device_errors(dev)
+        with pytest.raises(DeviceError, match="refused to launch"):
+            b200_fused_attention(q, k, v, None, True)
+        with pytest.raises(DeviceError):
+            module(x, None, causal=True)
+        with pytest.raises(DeviceError):
+            decoder(x)
+        clear_device_errors(dev)
+        check_device_errors(dev)
+        ref = reference_attention(q.cpu(), k.cpu(), v.cpu(), None, True, 128 ** -0.5)
+        assert_close(b200_fused_attention(q, k, v, None, True), ref, "after clearing")
+        assert torch.isfinite(decoder(x).float()).all()
+    assert read_device_errors(dev) == 0
