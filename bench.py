@@ -45,6 +45,9 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # N = 8); "ns" is the north-star shape.
 WORKLOADS = {
     "cfg1": dict(B=2, H=8, S=512, D=64, causal=True, masked=False, shard="batch"),
+    # configs[0] in its own dtype: fp32 inputs on the fp32 instance (TF32 products)
+    "cfg1f32": dict(B=2, H=8, S=512, D=64, causal=True, masked=False, shard="batch",
+                    dtype="float32"),
     "cfg2": dict(B=8, H=16, S=2048, D=128, causal=True, masked=False, shard="batch"),
     "cfg3": dict(B=16, H=32, S=4096, D=128, causal=False, masked=True, shard="batch"),
     "cfg4": dict(B=1, H=32, S=32768, D=128, causal=True, masked=False, shard="heads"),
@@ -67,7 +70,8 @@ def cfg_dtype(cfg: dict):
 
 
 def dtype_tag(cfg: dict) -> str:
-    return {"bfloat16": "bf16", "float16": "fp16"}[cfg.get("dtype", "bfloat16")]
+    return {"bfloat16": "bf16", "float16": "fp16", "float32": "fp32 (tf32 products)"}[
+        cfg.get("dtype", "bfloat16")]
 
 
 def load_peaks() -> tuple[dict, str]:

@@ -37,10 +37,14 @@ extern "C" {
 
 #define B200_ATTN_ABI_VERSION 2
 
-/* Element types of q, k, v and the output. */
+/* Element types of q, k, v and the output.  fp32 inputs are multiplied on the
+ * tensor cores as TF32 (10-bit mantissa products, fp32 accumulation), the
+ * reference's fp32 tiled kernel's precision (model/triton_fused_attention.py:
+ * 235-356); the softmax and the output stay fp32. */
 enum {
   B200_ATTN_DTYPE_BF16 = 0,
-  B200_ATTN_DTYPE_FP16 = 1
+  B200_ATTN_DTYPE_FP16 = 1,
+  B200_ATTN_DTYPE_FP32 = 2
 };
 
 /* Return codes.  Entry points never abort the process. */
@@ -110,7 +114,8 @@ typedef struct b200_attn_fwd_params {
 B200_ATTN_API int32_t b200_attn_abi_version(void);
 
 /* Host-only envelope query: 1 when the kernel computes (dtype, head_dim) for
- * the given causal/mask flags (head_dim any multiple of 8 up to 128), else 0.
+ * the given causal/mask flags (bf16/fp16: head_dim any multiple of 8 up to 128;
+ * fp32: any multiple of 8 up to 64), else 0.
  * Makes no CUDA call.  Head dims below 64 (above 64) run the 64-wide (128-wide)
  * kernel instance with the missing columns read as zeros by TMA; the result is
  * that of the true head dim.

@@ -16,6 +16,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libb200_attention.so"
 
 DTYPE_BF16 = 0
 DTYPE_FP16 = 1
+DTYPE_FP32 = 2  # attention only: TF32 products, fp32 softmax and output
 
 OK = 0
 ERR_INVALID_ARGUMENT = 1

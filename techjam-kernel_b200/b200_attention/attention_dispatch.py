@@ -77,10 +77,19 @@ class FallbackReason(_TextEnum):
 
 # Envelope of the sm_100a kernel; the C ABI's b200_attn_query answers the same
 # question and a CPU test keeps the two in agreement.
-SM100_DTYPES = ("bfloat16", "float16")
-# Every multiple of 8 up to 128: narrower heads run the 64- or 128-wide kernel
-# instance with the missing columns read as zeros by TMA.
+SM100_DTYPES = ("bfloat16", "float16", "float32")
+# 16-bit: every multiple of 8 up to 128 (narrower heads run the 64- or
+# 128-wide kernel instance with the missing columns read as zeros by TMA);
+# fp32 (TF32 products): every multiple of 8 up to 64.
 SM100_HEAD_DIMS = tuple(range(8, 129, 8))
+SM100_FP32_HEAD_DIMS = tuple(range(8, 65, 8))
+
+
+def sm100_supports(dtype: str, head_dim: int) -> bool:
+    """Whether the sm_100a kernel computes attention for (dtype, head_dim)."""
+    if dtype == "float32":
+        return head_dim in SM100_FP32_HEAD_DIMS
+    return dtype in SM100_DTYPES and head_dim in SM100_HEAD_DIMS
 SM100_CAPABILITY_MAJOR = 10
 # Launch shape of the sm_100a kernel (the C ABI's b200_attn_launch_shape
 # reports the same values; a CPU test keeps the two in agreement): 128-row
@@ -92,9 +101,12 @@ SM100_BLOCK_N = 128
 SM100_NUM_WARPS = 11
 
 
-def sm100_ring_slots(head_dim: int) -> int:
-    """K/V ring slots of the kernel instance that serves ``head_dim``: the
-    64-wide instance (head dims up to 64) holds 10, the 128-wide one 5."""
+def sm100_ring_slots(head_dim: int, dtype: str = "bfloat16") -> int:
+    """K/V ring slots of the kernel instance that serves (dtype, head_dim):
+    the 16-bit 64-wide instance (head dims up to 64) holds 10, the 128-wide
+    one and the fp32 instance (32 KB tiles) 5."""
+    if dtype == "float32":
+        return 5
     return 10 if head_dim <= 64 else 5
 
 
@@ -260,13 +272,14 @@ def _rule_matches(rule: tuple, spec: AttentionModelSpec, dtype: str) -> bool:
                  spec.num_layers) == (seq, d_model, heads, ffn, layers))
 
 
-def _sm100_launch(head_dim: int) -> KernelLaunch:
+def _sm100_launch(head_dim: int, dtype: str = "bfloat16") -> KernelLaunch:
     # num_stages = K/V ring slots (one K or one V tile per slot)
     return KernelLaunch(block_m=SM100_BLOCK_M, block_n=SM100_BLOCK_N, num_warps=SM100_NUM_WARPS,
-                        num_stages=sm100_ring_slots(head_dim), output_layout="bshd")
+                        num_stages=sm100_ring_slots(head_dim, dtype), output_layout="bshd")
 
 
-def _published_launch(mode: AttentionMode, spec: AttentionModelSpec) -> Optional[KernelLaunch]:
+def _published_launch(mode: AttentionMode, spec: AttentionModelSpec,
+                      dtype: str = "bfloat16") -> Optional[KernelLaunch]:
     """Launch metadata the reference attaches per mode (reference :303-354)."""
     S, D = spec.sequence_length, spec.head_dim
     if mode in (_M.FP16_FULL_ROW, _M.BF16_FULL_ROW):
@@ -294,7 +307,7 @@ def _published_launch(mode: AttentionMode, spec: AttentionModelSpec) -> Optional
     if mode in (_M.FP16_BLOCKED_EXACT, _M.BF16_BLOCKED_EXACT):
         return KernelLaunch(query_block_size=16, output_layout="bhsd")
     if mode == _M.SM100_FUSED:
-        return _sm100_launch(D)
+        return _sm100_launch(D, dtype)
     return None
 
 
@@ -335,7 +348,7 @@ def _sm100_reason(spec: AttentionModelSpec, rt: AttentionRuntime) -> Optional[Fa
         return shape
     if rt.dtype not in SM100_DTYPES:
         return FallbackReason.UNSUPPORTED_DTYPE
-    if spec.head_dim not in SM100_HEAD_DIMS:
+    if not sm100_supports(rt.dtype, spec.head_dim):
         return FallbackReason.UNVALIDATED_SHAPE
     return None
 
@@ -389,7 +402,7 @@ def _exact(index: int, dtype: str, reason: FallbackReason, explanation: str) -> 
 
 
 def _plan(index: int, mode: AttentionMode, spec: AttentionModelSpec,
-          explanation: Optional[str] = None) -> AttentionPlan:
+          explanation: Optional[str] = None, dtype: str = "bfloat16") -> AttentionPlan:
     """Attach family, launch and residual-stack reasons (reference :471-510)."""
     reason = None
     if mode == _M.FP32_BASELINE_EXACT and spec.d_model == 1024 and spec.num_heads == 4:
@@ -400,7 +413,8 @@ def _plan(index: int, mode: AttentionMode, spec: AttentionModelSpec,
         explanation = "FP32 D=128 Gluon candidate regressed the protected benchmark"
     elif mode in (_M.FP32_BASELINE_EXACT, _M.FP16_BLOCKED_EXACT):
         reason = FallbackReason.RESIDUAL_STACK_POLICY
-    return AttentionPlan(index, _FAMILY[mode], mode, _published_launch(mode, spec), reason, explanation)
+    return AttentionPlan(index, _FAMILY[mode], mode, _published_launch(mode, spec, dtype), reason,
+                         explanation)
 
 
 @lru_cache(maxsize=256)
@@ -411,7 +425,8 @@ def _select_cached(spec: AttentionModelSpec, rt: AttentionRuntime, scope: PlanSc
         reason = _sm100_reason(spec, rt)
         if reason is None:
             text = "sm_100a tcgen05/TMEM fused attention kernel"
-            return AttentionStackPlan(tuple(_plan(i, _M.SM100_FUSED, spec, text) for i in layers))
+            return AttentionStackPlan(tuple(_plan(i, _M.SM100_FUSED, spec, text, rt.dtype)
+                                            for i in layers))
         text = _REASON_TEXT.get(reason, "outside the sm_100a kernel envelope")
         return AttentionStackPlan(tuple(_exact(i, rt.dtype, reason, text) for i in layers))
 

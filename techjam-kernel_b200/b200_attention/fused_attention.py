@@ -27,12 +27,19 @@ import torch
 
 from . import _native
 
-SUPPORTED_DTYPES = {torch.bfloat16: _native.DTYPE_BF16, torch.float16: _native.DTYPE_FP16}
+# Element types of the block's linear and LayerNorm kernels (16-bit only).
+SIXTEEN_BIT_DTYPES = {torch.bfloat16: _native.DTYPE_BF16, torch.float16: _native.DTYPE_FP16}
+# Element types of the attention kernel: fp32 inputs run the fp32 instance,
+# whose products are TF32 (the reference's fp32 tiled kernel's precision,
+# model/triton_fused_attention.py:235-356) with an fp32 softmax and output.
+SUPPORTED_DTYPES = {**SIXTEEN_BIT_DTYPES, torch.float32: _native.DTYPE_FP32}
 # Every multiple of 8 up to 128.  The kernel's 64- and 128-wide instances read
 # the missing columns of narrower heads as zeros through TMA (zero columns add
 # nothing to Q K^T and P V) and its output store clips them; the softmax scale
 # stays that of the true head dim.  No padded copies are made.
 SUPPORTED_HEAD_DIMS = tuple(range(8, 129, 8))
+# fp32: multiples of 8 up to 64 (one 64-wide fp32 instance)
+FP32_HEAD_DIMS = tuple(range(8, 65, 8))
 NATIVE_HEAD_DIMS = SUPPORTED_HEAD_DIMS
 BLOCK_M = 128  # query rows per tile (two tiles per CTA)
 BLOCK_N = 128  # keys per K/V tile
@@ -83,7 +90,10 @@ def unsupported_reason(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> Opt
     if q.device.type != "cuda":
         return "inputs must be CUDA tensors"
     if q.dtype not in SUPPORTED_DTYPES:
-        return f"dtype {q.dtype} is outside the kernel envelope (bfloat16, float16)"
+        return f"dtype {q.dtype} is outside the kernel envelope (bfloat16, float16, float32)"
+    if q.dtype == torch.float32 and q.shape[-1] not in FP32_HEAD_DIMS:
+        return (f"head_dim {q.shape[-1]} is outside the kernel envelope for float32 "
+                "(multiples of 8 up to 64)")
     if q.shape[-1] not in SUPPORTED_HEAD_DIMS:
         return (f"head_dim {q.shape[-1]} is outside the kernel envelope "
                 "(multiples of 8 up to 128)")

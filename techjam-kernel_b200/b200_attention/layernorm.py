@@ -19,7 +19,7 @@ from typing import Optional
 import torch
 
 from . import _native
-from .fused_attention import SUPPORTED_DTYPES, raise_for_code
+from .fused_attention import SIXTEEN_BIT_DTYPES, raise_for_code
 
 MAX_COLS = 4096
 
@@ -32,7 +32,7 @@ assert _LN_LAYOUT.size == ctypes.sizeof(_native.LayerNormParams)
 
 def layer_norm_supported(x: torch.Tensor, weight: Optional[torch.Tensor]) -> bool:
     cols = x.shape[-1]
-    return (x.is_cuda and x.dtype in SUPPORTED_DTYPES and cols % 8 == 0 and 0 < cols <= MAX_COLS
+    return (x.is_cuda and x.dtype in SIXTEEN_BIT_DTYPES and cols % 8 == 0 and 0 < cols <= MAX_COLS
             and (weight is None or (weight.dtype == x.dtype and weight.device == x.device)))
 
 
@@ -89,7 +89,7 @@ def _layer_norm(x, addend, weight, bias, eps):
     if x.dim() < 1:
         raise ValueError("x must have at least one dimension")
     cols = x.shape[-1]
-    if x.dtype not in SUPPORTED_DTYPES:
+    if x.dtype not in SIXTEEN_BIT_DTYPES:
         raise ValueError(f"b200_layer_norm supports bfloat16 and float16, got {x.dtype}")
     if cols % 8 or cols > MAX_COLS or cols == 0:
         raise ValueError(f"b200_layer_norm needs a last dimension that is a multiple of 8 up to "
@@ -114,7 +114,7 @@ def _layer_norm(x, addend, weight, bias, eps):
     p = _native.LayerNormParams()
     _LN_LAYOUT.pack_into(p, 0, x2.data_ptr(), w.data_ptr() if w is not None else 0,
                          b.data_ptr() if b is not None else 0, y2.data_ptr(), x2.shape[0], cols,
-                         x2.stride(0), y2.stride(0), float(eps), SUPPORTED_DTYPES[x.dtype],
+                         x2.stride(0), y2.stride(0), float(eps), SIXTEEN_BIT_DTYPES[x.dtype],
                          a2.data_ptr() if a2 is not None else 0,
                          s2.data_ptr() if s2 is not None else 0,
                          a2.stride(0) if a2 is not None else 0,

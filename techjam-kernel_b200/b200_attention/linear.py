@@ -29,7 +29,7 @@ from typing import Optional
 import torch
 
 from . import _native
-from .fused_attention import SUPPORTED_DTYPES, device_error_word, raise_for_code
+from .fused_attention import SIXTEEN_BIT_DTYPES, device_error_word, raise_for_code
 
 # b200_linear_params packed in one call (layout checked against the ctypes
 # mirror at import): six pointers, m n k, four row strides, dtype, activation,
@@ -46,7 +46,7 @@ _ACTIVATIONS = {None: _native.LINEAR_ACT_NONE, "none": _native.LINEAR_ACT_NONE,
 
 def linear_supported(x: torch.Tensor, weight: torch.Tensor) -> bool:
     """True when ``b200_linear`` accepts these operands (device, dtype, sizes)."""
-    return (x.is_cuda and x.dtype in SUPPORTED_DTYPES and weight.dtype == x.dtype
+    return (x.is_cuda and x.dtype in SIXTEEN_BIT_DTYPES and weight.dtype == x.dtype
             and weight.device == x.device and weight.dim() == 2
             and weight.shape[1] == x.shape[-1] and weight.shape[0] % 8 == 0
             and weight.shape[1] % 8 == 0)
@@ -85,7 +85,7 @@ def b200_linear(
     n, k = weight.shape
     if x.shape[-1] != k:
         raise ValueError(f"x has {x.shape[-1]} features, weight expects {k}")
-    if x.dtype not in SUPPORTED_DTYPES:
+    if x.dtype not in SIXTEEN_BIT_DTYPES:
         raise ValueError(f"b200_linear supports bfloat16 and float16, got {x.dtype}")
     tensors = [("weight", weight), ("bias", bias), ("residual", residual)]
     for name, t in tensors:
@@ -133,7 +133,7 @@ def b200_linear(
         p, 0, x2.data_ptr(), w2.data_ptr(), b1.data_ptr() if b1 is not None else 0,
         r2.data_ptr() if r2 is not None else 0, m1.data_ptr() if m1 is not None else 0,
         y2.data_ptr(), x2.shape[0], n, k, x2.stride(0), w2.stride(0),
-        r2.stride(0) if r2 is not None else 0, y2.stride(0), SUPPORTED_DTYPES[x.dtype],
+        r2.stride(0) if r2 is not None else 0, y2.stride(0), SIXTEEN_BIT_DTYPES[x.dtype],
         _ACTIVATIONS[activation], _MASKED_ROWS[masked_rows], 0,
         device_error_word(x.device).data_ptr())
 

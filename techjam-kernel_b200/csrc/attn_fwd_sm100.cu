@@ -122,22 +122,28 @@ struct KernelArgs {
   int32_t skip_load;     // stall self-test only: K/V load left out (see b200_attn_selftest_stall)
 };
 
-// Compile-time shape of one kernel instance.
-template <int D_, int BN_, int PB_, int NSLOT_, bool SHARED_S_>
+// Compile-time shape of one kernel instance.  ELEM is the element size: 2
+// for bf16/fp16 (kind::f16 products), 4 for fp32 (kind::tf32 products).
+template <int D_, int BN_, int PB_, int NSLOT_, bool SHARED_S_, int ELEM_ = 2>
 struct Cfg {
   static constexpr int D = D_;          // head dim
   static constexpr int BN = BN_;        // keys per K/V tile
   static constexpr int PB = PB_;        // P buffers per query tile
   static constexpr int NSLOT = NSLOT_;  // K/V ring slots (one K or V tile each)
   static constexpr bool kSharedS = SHARED_S_;  // one S buffer for both query tiles
+  static constexpr int ELEM = ELEM_;
   static constexpr int kSBufs = kSharedS ? 1 : 2;
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
   static_assert(BN == 64 || BN == 128, "BN 64 or 128");
-  static constexpr int kChunks = D / 64;              // 128-byte swizzle chunks per row
+  static_assert(ELEM == 2 || ELEM == 4, "16- or 32-bit elements");
+  static constexpr int kChunkCols = 128 / ELEM;       // elements per 128-byte swizzle row
+  static constexpr int kChunks = D / kChunkCols;      // 128-byte swizzle chunks per row
+  static constexpr int kKStep = 32 / ELEM;            // K elements per tcgen05.mma
+  static constexpr int kPCols = BN * ELEM / 4;        // TMEM columns of one P buffer
   static constexpr int kQChunkBytes = kBlockM * 128;  // one chunk of a 128-row tile
   static constexpr int kKVChunkBytes = BN * 128;      // one chunk of a BN-row tile
-  static constexpr int kQTileBytes = kBlockM * D * 2;
-  static constexpr int kKVTileBytes = BN * D * 2;
+  static constexpr int kQTileBytes = kBlockM * D * ELEM;
+  static constexpr int kKVTileBytes = BN * D * ELEM;
   static constexpr int kOffQ = 0;
   static constexpr int kOffRing = 2 * kQTileBytes;
   static constexpr int kOffBar = kOffRing + NSLOT * kKVTileBytes;
@@ -158,12 +164,12 @@ struct Cfg {
   // TMEM columns
   __host__ __device__ static constexpr uint32_t col_s(int i) { return kSharedS ? 0u : BN * i; }
   __host__ __device__ static constexpr uint32_t col_p(int i, int b) {
-    return kSBufs * BN + (i * PB + b) * (BN / 2);
+    return kSBufs * BN + (i * PB + b) * kPCols;
   }
   __host__ __device__ static constexpr uint32_t col_o(int i) {
-    return kSBufs * BN + PB * BN + D * i;
+    return kSBufs * BN + 2 * PB * kPCols + D * i;
   }
-  static_assert(kSBufs * BN + PB * BN + 2 * D <= 512, "TMEM budget");
+  static_assert(kSBufs * BN + 2 * PB * kPCols + 2 * D <= 512, "TMEM budget");
   // Query tiles whose visible keys all lie in the first kExactKeys keys take
   // the exact-rounding path (keys held in registers across <= 2 tiles).
   static constexpr int kExactKeys = 128;
@@ -182,13 +188,15 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
-// x rounded to the input dtype and widened back to fp32.
-template <bool BF16>
+// x rounded to the input dtype and widened back to fp32 (fp32: x itself).
+template <int DT>
 __device__ __forceinline__ float round_to_input(float x) {
-  if constexpr (BF16) {
+  if constexpr (DT == B200_ATTN_DTYPE_BF16) {
     return __bfloat162float(__float2bfloat16_rn(x));
-  } else {
+  } else if constexpr (DT == B200_ATTN_DTYPE_FP16) {
     return __half2float(__float2half_rn(x));
+  } else {
+    return x;
   }
 }
 
@@ -371,7 +379,7 @@ __device__ __forceinline__ void mask_row(uint32_t (&s)[N], int lim, const uint32
 // kStallProbe (self-test instance only): K/V load number args.skip_load of
 // every CTA is announced to its barrier but never issued, so the pipeline
 // waits on it run out and exercise the abort path.
-template <class C, bool kCausal, bool kMask, bool kBF16, bool kStallProbe = false>
+template <class C, bool kCausal, bool kMask, int kDtype, bool kStallProbe = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
@@ -379,6 +387,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap tm_o, const KernelArgs args) {
   constexpr int D = C::D, BN = C::BN, PB = C::PB, NSLOT = C::NSLOT;
   constexpr int kMaskWords = BN / 32;
+  constexpr bool kBF16 = kDtype == B200_ATTN_DTYPE_BF16;
+  constexpr bool kTF32 = kDtype == B200_ATTN_DTYPE_FP32;  // fp32 inputs, TF32 products
+  static_assert(kTF32 == (C::ELEM == 4), "fp32 runs the 32-bit instance");
+  constexpr int kCC = C::kChunkCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -424,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     return a >= lo && a + bytes <= hi && ((a - sbase) & 1023u) == 0u;
   };
   auto coord_ok = [&](int x, int row, int hh, int bb, int row_hi) {
-    return x >= 0 && x + 64 <= D && (x & 63) == 0 && row >= 0 && row < row_hi && hh >= 0 &&
+    return x >= 0 && x + kCC <= D && (x % kCC) == 0 && row >= 0 && row < row_hi && hh >= 0 &&
            hh < args.heads && bb >= 0 && bb < args.batch;
   };
 
@@ -473,10 +485,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = q0 + threadIdx.x;
       if (row < S) {
         uint4* dst = reinterpret_cast<uint4*>(
-            reinterpret_cast<uint16_t*>(args.o) + static_cast<int64_t>(b) * args.o_sb +
-            static_cast<int64_t>(h) * args.o_sh + static_cast<int64_t>(row) * args.o_ss);
+            reinterpret_cast<uint8_t*>(args.o) +
+            C::ELEM * (static_cast<int64_t>(b) * args.o_sb + static_cast<int64_t>(h) * args.o_sh +
+                       static_cast<int64_t>(row) * args.o_ss));
 #pragma unroll
-        for (int c = 0; c < args.head_dim / 8; ++c) dst[c] = make_uint4(0u, 0u, 0u, 0u);
+        for (int c = 0; c < args.head_dim * C::ELEM / 16; ++c) dst[c] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
     return;
@@ -512,8 +525,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < C::kChunks; ++c) {
           const uint32_t dst = sbase + C::kOffQ + i * C::kQTileBytes + c * C::kQChunkBytes;
           if (chk(tile_ok(dst, C::kQChunkBytes, sbase + C::kOffQ, sbase + C::kOffRing) &&
-                  coord_ok(64 * c, q0 + kBlockM * i, h, b, args.num_q_blocks * kRowsPerCta)))
-            ptx::tma_load_4d(dst, &tm_q, bar(C::kBarQ), 64 * c, q0 + kBlockM * i, h, b);
+                  coord_ok(kCC * c, q0 + kBlockM * i, h, b, args.num_q_blocks * kRowsPerCta)))
+            ptx::tma_load_4d(dst, &tm_q, bar(C::kBarQ), kCC * c, q0 + kBlockM * i, h, b);
         }
       uint32_t L = 0;
       bool ok = true;
@@ -534,8 +547,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < C::kChunks; ++c) {
             const uint32_t dst = sbase + C::kOffRing + s * C::kKVTileBytes + c * C::kKVChunkBytes;
             if (chk(tile_ok(dst, C::kKVChunkBytes, sbase + C::kOffRing, sbase + C::kOffBar) &&
-                    coord_ok(64 * c, BN * j, h, b, S)))
-              ptx::tma_load_4d(dst, tm, bar(C::kBarSlotFull + s), 64 * c, BN * j, h, b);
+                    coord_ok(kCC * c, BN * j, h, b, S)))
+              ptx::tma_load_4d(dst, tm, bar(C::kBarSlotFull + s), kCC * c, BN * j, h, b);
           }
           ++L;
         }
@@ -559,7 +572,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // buffer were copied to registers by their softmax warpgroup.  With one
     // shared S buffer the occupancy order is S0(0), S1(0), S0(1), S1(1), ...
     if (lane == 0) {
-      constexpr uint32_t id_qk = ptx::idesc_f16(kBF16, kBlockM, BN, false);
+      constexpr uint32_t id_qk =
+          kTF32 ? ptx::idesc_tf32(kBlockM, BN, false) : ptx::idesc_f16(kBF16, kBlockM, BN, false);
       bool ok = wait_bar(bar(C::kBarQ), 0, abort_flag, args.err);
       int prev_i[2] = {-1, -1}, prev_j[2] = {-1, -1};  // last occupant per S buffer
       for (int j = 0; ok && j < n_max; ++j) {
@@ -585,12 +599,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          // 32 bytes of K per product: four products per 128-byte swizzle row
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
+          for (int kk = 0; kk < D / C::kKStep; ++kk) {
             const uint32_t qo = (kk >> 2) * C::kQChunkBytes + (kk & 3) * 32;
             const uint32_t ko = (kk >> 2) * C::kKVChunkBytes + (kk & 3) * 32;
-            ptx::tc_mma_ss(tmem + C::col_s(i), ptx::smem_desc_sw128(qaddr + qo, 16, 1024),
-                           ptx::smem_desc_sw128(kaddr + ko, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
+            const uint64_t qd = ptx::smem_desc_sw128(qaddr + qo, 16, 1024);
+            const uint64_t kd = ptx::smem_desc_sw128(kaddr + ko, 16, 1024);
+            if constexpr (kTF32)
+              ptx::tc_mma_ss_tf32(tmem + C::col_s(i), qd, kd, id_qk, kk > 0 ? 1u : 0u);
+            else
+              ptx::tc_mma_ss(tmem + C::col_s(i), qd, kd, id_qk, kk > 0 ? 1u : 0u);
           }
           ptx::tc_commit(bar(C::kBarSFull + i));
         }
@@ -610,7 +629,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // O_i += P_i(j) V(j): A = P from TMEM, B = V (MN-major, D contiguous),
     // issued as soon as the softmax warpgroup has written P_i(j).
     if (lane == 0) {
-      constexpr uint32_t id_pv = ptx::idesc_f16(kBF16, kBlockM, D, true);
+      constexpr uint32_t id_pv =
+          kTF32 ? ptx::idesc_tf32(kBlockM, D, true) : ptx::idesc_f16(kBF16, kBlockM, D, true);
       bool ok = true;
       for (int j = 0; ok && j < n_max; ++j) {
         const uint32_t vL = 2u * j + 1u, vs = vL % NSLOT;
@@ -626,17 +646,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ptx::tc_fence_after();
           if (!chk(tile_ok(vaddr, C::kKVTileBytes, sbase + C::kOffRing, sbase + C::kOffBar) &&
-                   C::col_p(i, j % PB) + BN / 2 <= kTmemCols && C::col_o(i) + D <= kTmemCols)) {
+                   C::col_p(i, j % PB) + C::kPCols <= kTmemCols && C::col_o(i) + D <= kTmemCols)) {
             ok = false;
             break;
           }
           const uint32_t pcol = tmem + C::col_p(i, j % PB);
+          // kKStep keys per product: kKStep rows of V (128 bytes each) and
+          // 8 TMEM columns of P (16-bit pairs, or single fp32 values)
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
+          for (int kk = 0; kk < BN / C::kKStep; ++kk) {
             const uint64_t bdesc =
-                ptx::smem_desc_sw128(vaddr + kk * 2048, C::kKVChunkBytes, 1024);
-            ptx::tc_mma_ts(tmem + C::col_o(i), pcol + kk * 8, bdesc, id_pv,
-                           (j > 0 || kk > 0) ? 1u : 0u);
+                ptx::smem_desc_sw128(vaddr + kk * (C::kKStep * 128), C::kKVChunkBytes, 1024);
+            if constexpr (kTF32) {
+              // fp32 V is MN-major in the 32-byte-atom swizzle: 4-row K groups
+              const uint64_t vdesc = ptx::smem_desc_sw128_base32(vaddr + kk * (C::kKStep * 128),
+                                                                 C::kKVChunkBytes, 512);
+              ptx::tc_mma_ts_tf32(tmem + C::col_o(i), pcol + kk * 8, vdesc, id_pv,
+                                  (j > 0 || kk > 0) ? 1u : 0u);
+            } else {
+              ptx::tc_mma_ts(tmem + C::col_o(i), pcol + kk * 8, bdesc, id_pv,
+                             (j > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           ptx::tc_commit(bar(C::kBarPVDone + i * PB + (j % PB)));
           if (j == n_tiles[i] - 1) ptx::tc_commit(bar(C::kBarOFull + i));
@@ -737,7 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < NE; ++k) {
           const float v =
-              round_to_input<kBF16>(round_to_input<kBF16>(__uint_as_float(sr[k])) * scale);
+              round_to_input<kDtype>(round_to_input<kDtype>(__uint_as_float(sr[k])) * scale);
           sr[k] = __float_as_uint(v);
           mx = fmaxf(mx, v);
         }
@@ -753,16 +783,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < C::kExactTiles; ++j) {
           if (j < n) {
-            uint32_t pk[BN / 2];
-#pragma unroll
-            for (int e = 0; e < BN / 2; ++e)
-              pk[e] = pack2<kBF16>(__uint_as_float(sr[j * BN + 2 * e]) * inv,
-                                   __uint_as_float(sr[j * BN + 2 * e + 1]) * inv);
             const uint32_t tP = tmem + lane_off + C::col_p(i, j % PB);
+            if constexpr (kTF32) {
+              // fp32 P, one column per key (the product reads it as TF32)
 #pragma unroll
-            for (int c = 0; c < BN / 64; ++c)
-              ptx::tmem_st_32x32b_x32(tP + 32 * c,
-                                      *reinterpret_cast<uint32_t(*)[32]>(&pk[32 * c]));
+              for (int k = 0; k < BN; ++k)
+                sr[j * BN + k] = __float_as_uint(__uint_as_float(sr[j * BN + k]) * inv);
+#pragma unroll
+              for (int c = 0; c < BN / 32; ++c)
+                ptx::tmem_st_32x32b_x32(tP + 32 * c,
+                                        *reinterpret_cast<uint32_t(*)[32]>(&sr[j * BN + 32 * c]));
+            } else {
+              uint32_t pk[BN / 2];
+#pragma unroll
+              for (int e = 0; e < BN / 2; ++e)
+                pk[e] = pack2<kBF16>(__uint_as_float(sr[j * BN + 2 * e]) * inv,
+                                     __uint_as_float(sr[j * BN + 2 * e + 1]) * inv);
+#pragma unroll
+              for (int c = 0; c < BN / 64; ++c)
+                ptx::tmem_st_32x32b_x32(tP + 32 * c,
+                                        *reinterpret_cast<uint32_t(*)[32]>(&pk[32 * c]));
+            }
             ptx::tmem_wait_st();
             warp_arrive(bar_p_full(j), lane);
           }
@@ -822,7 +863,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // p = 2^(s*scale*log2e - m); kPolyPer8 of every 8 on the FMA pipe
         // (ex2_poly), the rest on the MUFU; four independent partial sums.
         float sum[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t pk[BN / 2];
+        uint32_t pk[kTF32 ? 1 : BN / 2];  // packed 16-bit P (fp32 P overwrites sr in place)
 #pragma unroll
         for (int e = 0; e < BN / 2; ++e) {
           float x[2], p2[2];
@@ -845,7 +886,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             sum[e & 3] += p2[0] + p2[1];
           }
-          pk[e] = pack2<kBF16>(p2[0], p2[1]);
+          if constexpr (kTF32) {
+            sr[2 * e] = __float_as_uint(p2[0]);
+            sr[2 * e + 1] = __float_as_uint(p2[1]);
+          } else {
+            pk[e] = pack2<kBF16>(p2[0], p2[1]);
+          }
         }
         l_run += (sum[0] + sum[1]) + (sum[2] + sum[3]);
 
@@ -879,9 +925,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const uint32_t tP = tmem + lane_off + C::col_p(i, j % PB);
+        if constexpr (kTF32) {
 #pragma unroll
-        for (int c = 0; c < BN / 64; ++c)
-          ptx::tmem_st_32x32b_x32(tP + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&pk[32 * c]));
+          for (int c = 0; c < BN / 32; ++c)
+            ptx::tmem_st_32x32b_x32(tP + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < BN / 64; ++c)
+            ptx::tmem_st_32x32b_x32(tP + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&pk[32 * c]));
+        }
         ptx::tmem_wait_st();
         warp_arrive(bar_p_full(j), lane);
       }
@@ -914,19 +966,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t o[32];
         ptx::tmem_ld_32x32b_x32(tO + 32 * c, o);
         ptx::tmem_wait_ld();
+        // 16-byte pieces of the row: 8 packed 16-bit or 4 fp32 elements each
+        constexpr int kPer16 = 16 / C::ELEM;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 32 / kPer16; ++u) {
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            float a = __uint_as_float(o[8 * u + 2 * e]) * inv_l;
-            float bb = __uint_as_float(o[8 * u + 2 * e + 1]) * inv_l;
-            if (zero_row) a = bb = 0.f;
-            w[e] = pack2<kBF16>(a, bb);
+            if constexpr (kTF32) {
+              const float a = __uint_as_float(o[4 * u + e]) * inv_l;
+              w[e] = __float_as_uint(zero_row ? 0.f : a);
+            } else {
+              float a = __uint_as_float(o[8 * u + 2 * e]) * inv_l;
+              float bb = __uint_as_float(o[8 * u + 2 * e + 1]) * inv_l;
+              if (zero_row) a = bb = 0.f;
+              w[e] = pack2<kBF16>(a, bb);
+            }
           }
-          const int col = 32 * c + 8 * u;  // first element of this 16-byte chunk
-          const int cb = col >> 6;         // 64-column block
-          const int lc = (col & 63) >> 3;  // logical 16-byte chunk within the row
+          const int col = 32 * c + kPer16 * u;  // first element of this 16-byte piece
+          const int cb = col / kCC;             // 128-byte swizzle block of the row
+          const int lc = (col % kCC) / kPer16;  // logical 16-byte piece within the block
           const uint32_t addr = stage + cb * C::kQChunkBytes + rl * 128 + ((lc ^ (rl & 7)) << 4);
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[0]),
                        "r"(w[1]), "r"(w[2]), "r"(w[3])
@@ -940,8 +999,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cb = 0; cb < C::kChunks; ++cb) {
           const uint32_t src = stage + cb * C::kQChunkBytes;
           if (chk(tile_ok(src, C::kQChunkBytes, sbase + C::kOffQ, sbase + C::kOffRing) &&
-                  coord_ok(64 * cb, qstart, h, b, S)))
-            ptx::tma_store_4d(&tm_o, src, 64 * cb, qstart, h, b);
+                  coord_ok(kCC * cb, qstart, h, b, S)))
+            ptx::tma_store_4d(&tm_o, src, kCC * cb, qstart, h, b);
         }
         ptx::bulk_commit_group();
         ptx::bulk_wait_group_read_all();  // shared memory may go once the store has read it
@@ -965,6 +1024,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // run their exponentials at the same time and drift apart.
 using Cfg128 = Cfg<128, 128, 1, 5, true>;
 using Cfg64 = Cfg<64, 128, 1, 10, true>;
+// fp32 inputs (TF32 products), head dims up to 64: Q0/Q1 64 KB plus five
+// 32 KB K/V slots, and S | P0 P1 (128 fp32 columns each) | O0 O1 = 512 TMEM
+// columns, the same budgets as Cfg128.
+using CfgF32 = Cfg<64, 128, 1, 5, true, 4>;
 
 // ------------------------------------------------------------------- host
 // Text of the calling thread's last host-side failure, shared by every entry
@@ -995,12 +1058,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Any multiple of 8 up to 128.  The instance with D = 64 serves head dims up to
-// 64, D = 128 the rest: the tensor maps give the true head dim as the inner
-// extent, so the 64-column TMA boxes read zeros past it (Q K^T and P V are
+// 16-bit inputs: any multiple of 8 up to 128.  The instance with D = 64 serves
+// head dims up to 64, D = 128 the rest: the tensor maps give the true head dim
+// as the inner extent, so the TMA boxes read zeros past it (Q K^T and P V are
 // unchanged by zero columns) and the output store clips the columns past it.
-bool supported_head_dim(int64_t d) { return d >= 8 && d <= 128 && d % 8 == 0; }
+// fp32 inputs: any multiple of 8 up to 64, on the fp32 instance.
+bool supported_dtype(int32_t dtype) {
+  return dtype == B200_ATTN_DTYPE_BF16 || dtype == B200_ATTN_DTYPE_FP16 ||
+         dtype == B200_ATTN_DTYPE_FP32;
+}
+bool supported_head_dim(int32_t dtype, int64_t d) {
+  const int64_t hi = dtype == B200_ATTN_DTYPE_FP32 ? 64 : 128;
+  return d >= 8 && d <= hi && d % 8 == 0;
+}
 bool wide_head(int64_t d) { return d > 64; }
+int64_t elem_bytes(int32_t dtype) { return dtype == B200_ATTN_DTYPE_FP32 ? 4 : 2; }
 
 // Alignment rules of the 4-D TMA view {D, S, H, B}: 16-byte base, 16-byte
 // multiples for every stride whose dimension has extent > 1.
@@ -1010,37 +1082,43 @@ bool tensor_aligned(const void* ptr, const int64_t st[3], const b200_attn_fwd_pa
   for (int a = 0; a < 3; ++a) {
     if (ext[a] <= 1) continue;
     if (st[a] <= 0) return false;
-    if ((st[a] * 2) % 16 != 0) return false;
+    if ((st[a] * elem_bytes(p->dtype)) % 16 != 0) return false;
   }
   return true;
 }
 
-// 4-D tensor map {D, S, H, B} with a {64, box_rows, 1, 1} box, 128-byte swizzle.
+// 4-D tensor map {D, S, H, B} with a {128 bytes, box_rows, 1, 1} box (64
+// 16-bit or 32 fp32 elements), 128-byte swizzle.  `mn_major_tf32`: the box
+// lands in the 128-byte swizzle with 32-byte atoms, the only shared-memory
+// layout of an MN-major TF32 operand (fp32 V).
 int encode_map(CUtensorMap* m, const void* ptr, const int64_t st[3],
-               const b200_attn_fwd_params* p, uint32_t box_rows) {
+               const b200_attn_fwd_params* p, uint32_t box_rows, bool mn_major_tf32 = false) {
   auto fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled entry point unavailable");
     return B200_ATTN_ERR_LAUNCH;
   }
   const int64_t D = p->head_dim, S = p->seq_len, H = p->heads, B = p->batch;
+  const int64_t eb = elem_bytes(p->dtype);
   // Size-1 dimensions never move the address; give them a legal stride.
-  const int64_t fill = D * 2 * 16;
-  const int64_t s_seq = S > 1 ? st[2] * 2 : fill;
-  const int64_t s_head = H > 1 ? st[1] * 2 : fill;
-  const int64_t s_batch = B > 1 ? st[0] * 2 : fill;
+  const int64_t fill = D * eb * 16;
+  const int64_t s_seq = S > 1 ? st[2] * eb : fill;
+  const int64_t s_head = H > 1 ? st[1] * eb : fill;
+  const int64_t s_batch = B > 1 ? st[0] * eb : fill;
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S),
                         static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(B)};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_seq), static_cast<cuuint64_t>(s_head),
                            static_cast<cuuint64_t>(s_batch)};
-  cuuint32_t box[4] = {64, box_rows, 1, 1};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / eb), box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUtensorMapDataType dt = p->dtype == B200_ATTN_DTYPE_BF16
-                                     ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType dt = p->dtype == B200_ATTN_DTYPE_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : p->dtype == B200_ATTN_DTYPE_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const CUtensorMapSwizzle swz =
+      mn_major_tf32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
   CUresult r = fn(m, dt, 4, const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed");
     return B200_ATTN_ERR_LAUNCH;
@@ -1056,9 +1134,9 @@ struct DeviceState {
 };
 DeviceState g_dev[kMaxDevices];
 
-template <class Cf, bool Ca, bool M, bool BF, bool SP = false>
+template <class Cf, bool Ca, bool M, int DT, bool SP = false>
 int launch_one(const CUtensorMap maps[4], const KernelArgs& args, int device, cudaStream_t stream) {
-  auto kernel = attn_fwd_sm100_kernel<Cf, Ca, M, BF, SP>;
+  auto kernel = attn_fwd_sm100_kernel<Cf, Ca, M, DT, SP>;
   static std::once_flag attr_once[kMaxDevices];
   static cudaError_t attr_err[kMaxDevices];
   std::call_once(attr_once[device], [&] {
@@ -1080,20 +1158,30 @@ int launch_one(const CUtensorMap maps[4], const KernelArgs& args, int device, cu
   return B200_ATTN_OK;
 }
 
-template <class Cf>
+template <class Cf, int DT>
 int dispatch_flags(const CUtensorMap maps[4], const KernelArgs& a, const b200_attn_fwd_params* p,
                    int dev, cudaStream_t s) {
-  const bool c = p->causal != 0, m = p->key_mask != nullptr, bf = p->dtype == B200_ATTN_DTYPE_BF16;
+  const bool c = p->causal != 0, m = p->key_mask != nullptr;
   if (c) {
-    if (m) return bf ? launch_one<Cf, true, true, true>(maps, a, dev, s)
-                     : launch_one<Cf, true, true, false>(maps, a, dev, s);
-    return bf ? launch_one<Cf, true, false, true>(maps, a, dev, s)
-              : launch_one<Cf, true, false, false>(maps, a, dev, s);
+    return m ? launch_one<Cf, true, true, DT>(maps, a, dev, s)
+             : launch_one<Cf, true, false, DT>(maps, a, dev, s);
   }
-  if (m) return bf ? launch_one<Cf, false, true, true>(maps, a, dev, s)
-                   : launch_one<Cf, false, true, false>(maps, a, dev, s);
-  return bf ? launch_one<Cf, false, false, true>(maps, a, dev, s)
-            : launch_one<Cf, false, false, false>(maps, a, dev, s);
+  return m ? launch_one<Cf, false, true, DT>(maps, a, dev, s)
+           : launch_one<Cf, false, false, DT>(maps, a, dev, s);
+}
+
+// Kernel instance for (dtype, head_dim): its keys per K/V tile and ring slots.
+void instance_shape(int32_t dtype, int64_t head_dim, int* block_n, int* slots) {
+  if (dtype == B200_ATTN_DTYPE_FP32) {
+    *block_n = CfgF32::BN;
+    *slots = CfgF32::NSLOT;
+  } else if (wide_head(head_dim)) {
+    *block_n = Cfg128::BN;
+    *slots = Cfg128::NSLOT;
+  } else {
+    *block_n = Cfg64::BN;
+    *slots = Cfg64::NSLOT;
+  }
 }
 
 }  // namespace
@@ -1108,8 +1196,8 @@ extern "C" int32_t b200_attn_query(int32_t dtype, int64_t head_dim, int32_t caus
                                    int32_t has_mask) {
   (void)causal;
   (void)has_mask;
-  if (dtype != B200_ATTN_DTYPE_BF16 && dtype != B200_ATTN_DTYPE_FP16) return 0;
-  return supported_head_dim(head_dim) ? 1 : 0;
+  if (!supported_dtype(dtype)) return 0;
+  return supported_head_dim(dtype, head_dim) ? 1 : 0;
 }
 
 extern "C" const char* b200_attn_error_string(int32_t code) {
@@ -1137,12 +1225,13 @@ extern "C" int32_t b200_attn_launch_shape(int32_t dtype, int64_t head_dim, int32
                                           int32_t* rows_per_cta, int32_t* block_n,
                                           int32_t* num_warps, int32_t* ring_slots) {
   if (!b200_attn_query(dtype, head_dim, 0, 0)) return 0;
-  const bool wide = wide_head(head_dim);
+  int bn = 0, slots = 0;
+  instance_shape(dtype, head_dim, &bn, &slots);
   if (block_m) *block_m = kBlockM;
   if (rows_per_cta) *rows_per_cta = kRowsPerCta;
-  if (block_n) *block_n = wide ? Cfg128::BN : Cfg64::BN;
+  if (block_n) *block_n = bn;
   if (num_warps) *num_warps = kThreads / 32;
-  if (ring_slots) *ring_slots = wide ? Cfg128::NSLOT : Cfg64::NSLOT;
+  if (ring_slots) *ring_slots = slots;
   return 1;
 }
 
@@ -1153,9 +1242,8 @@ extern "C" int32_t b200_attn_check(const b200_attn_fwd_params* p) {
   if (p->batch * p->heads > (1ll << 24) || p->seq_len > (1ll << 30))
     return B200_ATTN_ERR_INVALID_ARGUMENT;
   if (!(p->scale > 0.f) || !std::isfinite(p->scale)) return B200_ATTN_ERR_INVALID_ARGUMENT;
-  if (p->dtype != B200_ATTN_DTYPE_BF16 && p->dtype != B200_ATTN_DTYPE_FP16)
-    return B200_ATTN_ERR_UNSUPPORTED;
-  if (!supported_head_dim(p->head_dim)) return B200_ATTN_ERR_UNSUPPORTED;
+  if (!supported_dtype(p->dtype)) return B200_ATTN_ERR_UNSUPPORTED;
+  if (!supported_head_dim(p->dtype, p->head_dim)) return B200_ATTN_ERR_UNSUPPORTED;
   if (p->zero_masked_queries && !p->key_mask) return B200_ATTN_ERR_INVALID_ARGUMENT;
   if (!tensor_aligned(p->q, p->q_stride, p) || !tensor_aligned(p->k, p->k_stride, p) ||
       !tensor_aligned(p->v, p->v_stride, p) || !tensor_aligned(p->o, p->o_stride, p))
@@ -1214,10 +1302,13 @@ int32_t prepare(const b200_attn_fwd_params* p, CUtensorMap maps[4], KernelArgs& 
     return B200_ATTN_ERR_DEVICE;
   }
 
-  const uint32_t kv_rows = wide_head(p->head_dim) ? Cfg128::BN : Cfg64::BN;
+  int bn = 0, slots = 0;
+  instance_shape(p->dtype, p->head_dim, &bn, &slots);
+  const uint32_t kv_rows = static_cast<uint32_t>(bn);
   if ((rc = encode_map(&maps[0], p->q, p->q_stride, p, kBlockM)) != B200_ATTN_OK ||
       (rc = encode_map(&maps[1], p->k, p->k_stride, p, kv_rows)) != B200_ATTN_OK ||
-      (rc = encode_map(&maps[2], p->v, p->v_stride, p, kv_rows)) != B200_ATTN_OK ||
+      (rc = encode_map(&maps[2], p->v, p->v_stride, p, kv_rows,
+                       p->dtype == B200_ATTN_DTYPE_FP32)) != B200_ATTN_OK ||
       (rc = encode_map(&maps[3], p->o, p->o_stride, p, kBlockM)) != B200_ATTN_OK)
     return rc;
 
@@ -1228,7 +1319,7 @@ int32_t prepare(const b200_attn_fwd_params* p, CUtensorMap maps[4], KernelArgs& 
   a.num_q_blocks = static_cast<int32_t>((p->seq_len + kRowsPerCta - 1) / kRowsPerCta);
   {
     const int64_t bh = p->batch * p->heads;
-    const int64_t kv_bytes = 4 * p->seq_len * p->head_dim;  // K and V of one head, 16-bit
+    const int64_t kv_bytes = 2 * elem_bytes(p->dtype) * p->seq_len * p->head_dim;  // K and V of one head
     // As few groups as the L2 budget allows, all of (nearly) equal size: a
     // small last group would start its heaviest query blocks late and
     // lengthen the tail (measured: -11 % for 4 heads of S = 32768).
@@ -1265,8 +1356,16 @@ extern "C" int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream) {
   const int32_t rc = prepare(p, maps, a, dev, guard);
   if (rc != B200_ATTN_OK) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (wide_head(p->head_dim)) return dispatch_flags<Cfg128>(maps, a, p, dev, s);
-  return dispatch_flags<Cfg64>(maps, a, p, dev, s);
+  switch (p->dtype) {
+    case B200_ATTN_DTYPE_FP32:
+      return dispatch_flags<CfgF32, B200_ATTN_DTYPE_FP32>(maps, a, p, dev, s);
+    case B200_ATTN_DTYPE_FP16:
+      return wide_head(p->head_dim) ? dispatch_flags<Cfg128, B200_ATTN_DTYPE_FP16>(maps, a, p, dev, s)
+                                    : dispatch_flags<Cfg64, B200_ATTN_DTYPE_FP16>(maps, a, p, dev, s);
+    default:
+      return wide_head(p->head_dim) ? dispatch_flags<Cfg128, B200_ATTN_DTYPE_BF16>(maps, a, p, dev, s)
+                                    : dispatch_flags<Cfg64, B200_ATTN_DTYPE_BF16>(maps, a, p, dev, s);
+  }
 }
 
 extern "C" int32_t b200_attn_selftest_stall(const b200_attn_fwd_params* p, int32_t skipped_load,
@@ -1281,6 +1380,6 @@ extern "C" int32_t b200_attn_selftest_stall(const b200_attn_fwd_params* p, int32
   const int32_t rc = prepare(p, maps, a, dev, guard);
   if (rc != B200_ATTN_OK) return rc;
   a.skip_load = skipped_load;
-  return launch_one<Cfg128, true, false, true, true>(maps, a, dev,
-                                                    reinterpret_cast<cudaStream_t>(stream));
+  return launch_one<Cfg128, true, false, B200_ATTN_DTYPE_BF16, true>(
+      maps, a, dev, reinterpret_cast<cudaStream_t>(stream));
 }

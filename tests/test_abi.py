@@ -73,11 +73,17 @@ def test_launch_counter_starts_without_gpu_work(lib):
 def test_query_agrees_with_planner_envelope(lib):
     """The C ABI and the planner agree on the head dims the kernel computes:
     every multiple of 8 up to 128."""
-    for dtype in (_native.DTYPE_BF16, _native.DTYPE_FP16, 7):
-        for d in (0, 4, 8, 12, 16, 32, 60, 64, 96, 120, 128, 136, 256):
-            supported = 1 if dtype in (0, 1) and d in SM100_HEAD_DIMS else 0
-            assert lib.b200_attn_query(dtype, d, 1, 0) == supported
+    from b200_attention.attention_dispatch import sm100_supports
+
+    names = {_native.DTYPE_BF16: "bfloat16", _native.DTYPE_FP16: "float16",
+             _native.DTYPE_FP32: "float32", 7: "float64"}
+    for dtype, name in names.items():
+        for d in (0, 4, 8, 12, 16, 32, 60, 64, 72, 96, 120, 128, 136, 256):
+            supported = 1 if sm100_supports(name, d) else 0
+            assert lib.b200_attn_query(dtype, d, 1, 0) == supported, (name, d)
     assert set(SM100_HEAD_DIMS) == set(range(8, 129, 8))
+    assert lib.b200_attn_query(_native.DTYPE_FP32, 64, 1, 0) == 1
+    assert lib.b200_attn_query(_native.DTYPE_FP32, 72, 1, 0) == 0
 
 
 def test_launch_shape_agrees_with_planner(lib):
@@ -87,11 +93,16 @@ def test_launch_shape_agrees_with_planner(lib):
     from b200_attention.attention_dispatch import (SM100_BLOCK_M, SM100_BLOCK_N, SM100_NUM_WARPS,
                                                    _sm100_launch)
 
-    for dtype in (_native.DTYPE_BF16, _native.DTYPE_FP16):
+    names = {_native.DTYPE_BF16: "bfloat16", _native.DTYPE_FP16: "float16",
+             _native.DTYPE_FP32: "float32"}
+    for dtype, name in names.items():
         for d in SM100_HEAD_DIMS:
             shape = _native.launch_shape(dtype, d)
+            if name == "float32" and d > 64:
+                assert shape is None
+                continue
             assert shape is not None, (dtype, d)
-            launch = _sm100_launch(d)
+            launch = _sm100_launch(d, name)
             assert (shape["block_m"], shape["block_n"], shape["num_warps"], shape["ring_slots"]) == (
                 launch.block_m, launch.block_n, launch.num_warps, launch.num_stages), (dtype, d)
             assert (shape["block_m"], shape["block_n"], shape["num_warps"]) == (
@@ -138,6 +149,7 @@ def test_check_accepts_valid_params(lib):
     (dict(scale=-1.0), _native.ERR_INVALID_ARGUMENT),
     (dict(scale=float("inf")), _native.ERR_INVALID_ARGUMENT),
     (dict(dtype=5), _native.ERR_UNSUPPORTED),
+    (dict(dtype=_native.DTYPE_FP32), _native.ERR_UNSUPPORTED),  # fp32 heads only up to 64
     (dict(head_dim=136), _native.ERR_UNSUPPORTED),
     (dict(head_dim=100), _native.ERR_UNSUPPORTED),
     (dict(q=0x10008), _native.ERR_ALIGNMENT),
@@ -145,6 +157,19 @@ def test_check_accepts_valid_params(lib):
 ])
 def test_check_rejects(lib, kw, code):
     assert _check(lib, _params(**kw)) == code
+
+
+def test_check_accepts_fp32_up_to_head_dim_64(lib):
+    p = _params(dtype=_native.DTYPE_FP32, head_dim=64)
+    for name in ("q_stride", "k_stride", "v_stride", "o_stride"):
+        getattr(p, name)[:] = (4 * 256 * 64, 256 * 64, 64)
+    assert _check(lib, p) == _native.OK
+    p.head_dim = 8  # 32-byte rows: 16-byte multiples for fp32
+    for name in ("q_stride", "k_stride", "v_stride", "o_stride"):
+        getattr(p, name)[:] = (4 * 256 * 8, 256 * 8, 8)
+    assert _check(lib, p) == _native.OK
+    getattr(p, "k_stride")[:] = (4 * 256 * 8, 256 * 8, 10)  # 40-byte rows
+    assert _check(lib, p) == _native.ERR_ALIGNMENT
 
 
 def test_check_rejects_unaligned_stride(lib):

@@ -38,15 +38,37 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("B,H,S,D,causal,lengths,zero_q", CASES)
-def test_checked_build_odd_shapes(B, H, S, D, causal, lengths, zero_q):
+# fp32 inputs (TF32 products) on the fp32 instance: head dims up to 64
+CASES_FP32 = [
+    (1, 1, 1, 64, True, None, False),
+    (2, 2, 33, 64, False, None, False),
+    (2, 1, 129, 64, True, None, False),
+    (3, 2, 700, 64, False, [700, 333, 1], True),
+    (1, 2, 1000, 64, True, None, False),
+    (2, 2, 300, 32, True, [300, 123], True),
+    (1, 3, 129, 8, False, None, False),
+    (2, 1, 257, 40, True, None, False),
+]
+
+
+def _case_id(c):
+    dtype, B, H, S, D, causal, lengths, zero_q = c
+    return f"{str(dtype).removeprefix('torch.')}-B{B}H{H}S{S}D{D}{'-causal' if causal else ''}" \
+           f"{'-mask' if lengths else ''}{'-zeroq' if zero_q else ''}"
+
+
+_ALL = [(torch.bfloat16, *c) for c in CASES] + [(torch.float32, *c) for c in CASES_FP32]
+
+
+@pytest.mark.parametrize("dtype,B,H,S,D,causal,lengths,zero_q", _ALL, ids=[_case_id(c) for c in _ALL])
+def test_checked_build_odd_shapes(dtype, B, H, S, D, causal, lengths, zero_q):
     dev = torch.device("cuda", 0)
     lib = _native.load_checked_library()
-    q, k, v = seeded_qkv((B, H, S, D), torch.bfloat16, 41 + S)
+    q, k, v = seeded_qkv((B, H, S, D), dtype, 41 + S)
     mask = prefix_mask(B, S, lengths) if lengths else None
     qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
     md = mask.to(dev) if mask is not None else None
-    out = torch.full((B, H, S, D), float("nan"), device=dev, dtype=torch.bfloat16)
+    out = torch.full((B, H, S, D), float("nan"), device=dev, dtype=dtype)
     read_device_errors(dev)
     params = make_params(qd, kd, vd, out, md, causal, D ** -0.5, zero_q, device_error_word(dev))
     rc = lib.b200_attn_fwd(ctypes.byref(params),
@@ -57,4 +79,4 @@ def test_checked_build_odd_shapes(B, H, S, D, causal, lengths, zero_q):
     ref = reference_attention(q, k, v, mask, causal, D ** -0.5)
     if zero_q:
         ref = zero_masked_rows(ref, mask)
-    assert_close(out, ref, f"checked B{B} H{H} S{S} D{D}")
+    assert_close(out, ref, f"checked {dtype} B{B} H{H} S{S} D{D}")

@@ -85,23 +85,26 @@ def test_long_causal_sampled_rows(name, shape):
 
 def test_kernel_against_reference_golden_outputs():
     """The reference's own outputs (tests/golden, produced by importing the
-    reference) for every case the kernel covers (bf16/fp16, D 64/128)."""
+    reference) for every case the kernel covers (bf16/fp16 at D 64/128, fp32 at
+    D 64)."""
     meta = json.loads((GOLDEN / "attention_cases.json").read_text())
     arrays = np.load(GOLDEN / "attention_cases.npz")
     checked = 0
     for case in meta["cases"]:
-        if case["dtype"] not in ("bfloat16", "float16") or case["shape"][3] not in (64, 128):
+        if case["shape"][3] not in (64, 128) or (case["dtype"] == "float32" and case["shape"][3] > 64):
             continue
         q, k, v, mask = load_case_inputs(case)
         out = _kernel(q, k, v, mask, case["causal"])
         keep = case["keep_heads"]
         if keep:
             out = out[:, :keep]
-        dt = torch.bfloat16 if case["dtype"] == "bfloat16" else torch.float16
-        golden = torch.from_numpy(arrays[case["name"]].copy()).view(dt)
+        dt = {"bfloat16": torch.bfloat16, "float16": torch.float16,
+              "float32": torch.float32}[case["dtype"]]
+        golden = torch.from_numpy(arrays[case["name"]].copy())
+        golden = golden if dt == torch.float32 else golden.view(dt)
         assert_close(out, golden, case["name"])
         checked += 1
-    assert checked >= 7
+    assert checked >= 8
 
 
 def test_autograd_routes_to_the_exact_path_on_cuda():

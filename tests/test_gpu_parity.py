@@ -211,3 +211,60 @@ def test_fp16_zero_masked_queries_bshd():
     out, ref = _run((2, 2, 640, 128), torch.float16, True, lengths=[640, 200], seed=53, zero_q=True,
                     bshd=True)
     assert_close(out, ref, "fp16 zero_q bshd")
+
+
+
+# fp32 inputs: the fp32 instance multiplies on the tensor cores as TF32 (the
+# precision of the reference's fp32 tiled kernel, model/triton_fused_attention.py:
+# 235-356) with an fp32 softmax and fp32 output; the oracle is exact fp32
+# attention in the reference's operation order, and the bound is the same
+# max-abs <= 2e-2 / mean-abs <= 2e-3 as for the 16-bit types.
+
+
+def test_fp32_cfg1_full():
+    """B2 H8 S512 D64 causal in fp32 (the reference's CPU dtype)."""
+    out, ref = _run((2, 8, 512, 64), torch.float32, True)
+    assert out.dtype == torch.float32
+    assert_close(out, ref, "fp32 cfg1")
+
+
+@pytest.mark.parametrize("D", [8, 16, 32, 64])
+@pytest.mark.parametrize("causal", [False, True])
+def test_fp32_head_dims(D, causal):
+    out, ref = _run((2, 3, 300, D), torch.float32, causal, lengths=[300, 123], seed=61)
+    assert_close(out, ref, f"fp32 D={D}")
+
+
+@pytest.mark.parametrize("S", [1, 33, 128, 129, 257])
+def test_fp32_partial_tiles(S):
+    out, ref = _run((2, 2, S, 64), torch.float32, True, seed=67)
+    assert_close(out, ref, f"fp32 S={S}")
+
+
+def test_fp32_small_head_full_row():
+    """The reference's fp32 D=8 small-head case (S <= 128, its Gluon kernel,
+    model/triton_gluon_attention.py:184-317): B4 H16 S128 D8."""
+    out, ref = _run((4, 16, 128, 8), torch.float32, True, seed=71)
+    assert_close(out, ref, "fp32 D=8 S=128")
+
+
+def test_fp32_long_causal():
+    """The reference's fp32 tiled envelope (causal, S >= 1024, D 32/64)."""
+    for D in (32, 64):
+        out, ref = _run((1, 4, 2048, D), torch.float32, True, seed=73)
+        assert_close(out, ref, f"fp32 S=2048 D={D}")
+
+
+def test_fp32_masks_nan_rows_zero_queries_and_bshd():
+    out, ref = _run((2, 1, 130, 64), torch.float32, False, lengths=[130, 0], seed=79)
+    assert torch.isnan(out[1]).all() and torch.isnan(ref[1]).all()
+    assert_close(out, ref, "fp32 nan rows")
+    out, ref = _run((3, 2, 600, 64), torch.float32, True, lengths=[600, 257, 1], seed=83,
+                    zero_q=True, bshd=True)
+    assert_close(out, ref, "fp32 zero_q bshd")
+
+
+def test_fp32_head_dim_above_64_is_refused():
+    ok = torch.zeros((1, 1, 64, 128), device=DEV, dtype=torch.float32)
+    with pytest.raises(ValueError, match="float32"):
+        b200_fused_attention(ok, ok, ok, None, True)

@@ -12,10 +12,10 @@ from pathlib import Path
 
 import pytest
 
-from b200_attention.attention_dispatch import (SM100_DTYPES, SM100_HEAD_DIMS, AttentionFamily,
+from b200_attention.attention_dispatch import (AttentionFamily,
                                                AttentionMode, AttentionModelSpec, AttentionRuntime,
                                                FallbackReason, PlanScope, clear_plan_cache,
-                                               select_attention_stack_plan)
+                                               select_attention_stack_plan, sm100_supports)
 
 PLANS = json.loads((Path(__file__).resolve().parent / "golden" / "planner_plans.json").read_text())
 
@@ -50,7 +50,7 @@ def test_reference_plans_reproduced(entry):
                          ids=lambda e: f"case{e['case']}-{e['dtype']}-{e['scope']}")
 def test_b200_plans(entry):
     spec, sp = _select(entry)
-    in_envelope = entry["dtype"] in SM100_DTYPES and spec.head_dim in SM100_HEAD_DIMS
+    in_envelope = sm100_supports(entry["dtype"], spec.head_dim)
     # the reference runs every B200 shape on its exact PyTorch path
     assert {l["reason"] for l in entry["layers"]} == {"cuda_capability"}
     if in_envelope:
@@ -73,7 +73,13 @@ def test_b200_gates():
     assert select_attention_stack_plan(spec, _rt()).layers[0].mode == AttentionMode.SM100_FUSED
     assert select_attention_stack_plan(spec, _rt("float16")).layers[0].mode == AttentionMode.SM100_FUSED
     fp32 = select_attention_stack_plan(spec, _rt("float32")).layers[0]
-    assert (fp32.mode, fp32.reason) == (AttentionMode.FP32_BASELINE_EXACT, FallbackReason.UNSUPPORTED_DTYPE)
+    # fp32 runs the TF32 instance for head dims up to 64 only
+    assert (fp32.mode, fp32.reason) == (AttentionMode.FP32_BASELINE_EXACT, FallbackReason.UNVALIDATED_SHAPE)
+    d64 = AttentionModelSpec(8, 2048, 1024, 16, 4096, 2, True)  # D = 64
+    fp32_64 = select_attention_stack_plan(d64, _rt("float32", d=1024)).layers[0]
+    assert fp32_64.mode == AttentionMode.SM100_FUSED and fp32_64.launch.num_stages == 5
+    assert select_attention_stack_plan(d64, _rt("float64", d=1024)).layers[0].reason == \
+        FallbackReason.UNSUPPORTED_DTYPE
     ag = select_attention_stack_plan(spec, _rt(autograd=True)).layers[0]
     assert (ag.mode, ag.reason) == (AttentionMode.EXACT_REFERENCE, FallbackReason.AUTOGRAD)
     mism = select_attention_stack_plan(spec, _rt(S=1024)).layers[0]
