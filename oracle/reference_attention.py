@@ -41,18 +41,56 @@ def reference_attention(
     scale: float,
 ) -> torch.Tensor:
     """Dense oracle; follows model/triton_fused_attention.py:1256-1285 step by step."""
-    seq_len = q.shape[2]
     q_ref = q.contiguous()
     k_ref = k.contiguous()
     v_ref = v.contiguous()
-    scores = torch.matmul(q_ref, k_ref.transpose(-2, -1)) * scale
+    scores = torch.matmul(q_ref, k_ref.transpose(-2, -1))
+    probabilities = reference_softmax(scores, valid_token_mask, scale, causal)
+    return torch.matmul(probabilities, v_ref)
+
+
+def reference_softmax(
+    scores: torch.Tensor,
+    valid_token_mask: Optional[torch.Tensor],
+    scale: float,
+    causal: bool,
+) -> torch.Tensor:
+    """The softmax stage of the value definition on unscaled scores ``[B, H, S, S]``
+    (model/triton_fused_attention.py:1272-1284; torch_transformer_benchmark.py:98-112):
+    the scale multiply in the scores' dtype, causal triu(1) and key-mask
+    positions set to -inf, fp32 softmax, rounded back to the dtype.  This is
+    also what the reference's row-softmax seam computes
+    (model/triton_softmax.py:19-96, 99-161), which takes the unscaled scores."""
+    seq_len = scores.shape[-1]
+    scores = scores * scale
     if causal:
-        causal_mask = torch.ones((seq_len, seq_len), device=q.device, dtype=torch.bool).triu(diagonal=1)
+        causal_mask = torch.ones((seq_len, seq_len), device=scores.device,
+                                 dtype=torch.bool).triu(diagonal=1)
         scores = scores.masked_fill(causal_mask, float("-inf"))
     if valid_token_mask is not None:
         scores = scores.masked_fill(~valid_token_mask[:, None, None, :], float("-inf"))
-    probabilities = torch.softmax(scores.float(), dim=-1).to(q.dtype)
-    return torch.matmul(probabilities, v_ref)
+    return torch.softmax(scores.float(), dim=-1).to(scores.dtype)
+
+
+def reference_softmax_rows(
+    scores_rows: torch.Tensor,
+    valid_token_mask: Optional[torch.Tensor],
+    scale: float,
+    causal: bool,
+    row_start: int,
+) -> torch.Tensor:
+    """``reference_softmax`` for the query rows ``[row_start, row_start + R)``
+    only (``scores_rows`` is ``[B, H, R, S]``), each element computed exactly as
+    in the dense form; the bounded form for long rows."""
+    rows, seq_len = scores_rows.shape[-2], scores_rows.shape[-1]
+    scores = scores_rows * scale
+    if causal:
+        r = torch.arange(row_start, row_start + rows, device=scores.device)[:, None]
+        c = torch.arange(seq_len, device=scores.device)[None, :]
+        scores = scores.masked_fill(c > r, float("-inf"))
+    if valid_token_mask is not None:
+        scores = scores.masked_fill(~valid_token_mask[:, None, None, :], float("-inf"))
+    return torch.softmax(scores.float(), dim=-1).to(scores.dtype)
 
 
 def reference_attention_rows(

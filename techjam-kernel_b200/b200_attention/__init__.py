@@ -5,8 +5,13 @@
 - ``B200FusedSelfAttention``: module adapter (reference: TritonFusedSelfAttention)
 - ``b200_linear``: the block's linear layers with their elementwise epilogues
   (bias, exact GELU, residual add, padded-row zeroing) fused into one kernel
+- ``b200_attention_softmax`` / ``B200SoftmaxSelfAttention``: the row softmax
+  over materialised scores (reference: triton_attention_softmax /
+  TritonSelfAttention, also exported under those names)
 """
 
 from .fused_attention import (DeviceError, b200_fused_attention, check_device_errors,  # noqa: F401
                               clear_device_errors, read_device_errors)
 from .linear import b200_linear  # noqa: F401
+from .softmax import (B200SoftmaxSelfAttention, TritonSelfAttention,  # noqa: F401
+                      b200_attention_softmax, triton_attention_softmax)

@@ -1,5 +1,5 @@
-"""ctypes binding of the C ABI in ``include/b200_attn.h``, ``include/b200_linear.h``
-and ``include/b200_layernorm.h``.
+"""ctypes binding of the C ABI in ``include/b200_attn.h``, ``include/b200_linear.h``,
+``include/b200_layernorm.h`` and ``include/b200_softmax.h``.
 
 This module is torch-free: it loads ``libb200_attention.so`` and describes the
 parameter struct.  The library is loaded from this directory only; a missing or
@@ -58,6 +58,13 @@ LAYERNORM_SYMBOLS = (
     "b200_layernorm_check",
     "b200_layernorm_fwd",
 )
+
+# Every symbol ``include/b200_softmax.h`` declares.
+SOFTMAX_SYMBOLS = (
+    "b200_softmax_check",
+    "b200_softmax_fwd",
+)
+SOFTMAX_MAX_SEQ = 65536
 
 LINEAR_ACT_NONE = 0
 LINEAR_ACT_GELU = 1
@@ -137,6 +144,24 @@ class LayerNormParams(ctypes.Structure):
     ]
 
 
+class SoftmaxParams(ctypes.Structure):
+    """Mirror of ``b200_softmax_params``."""
+
+    _fields_ = [
+        ("scores", ctypes.c_void_p),
+        ("probs", ctypes.c_void_p),
+        ("batch", ctypes.c_int64),
+        ("heads", ctypes.c_int64),
+        ("seq_len", ctypes.c_int64),
+        ("key_mask", ctypes.c_void_p),
+        ("mask_stride", ctypes.c_int64 * 2),
+        ("scale", ctypes.c_float),
+        ("dtype", ctypes.c_int32),
+        ("causal", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -175,6 +200,10 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.b200_layernorm_check.argtypes = [ctypes.POINTER(LayerNormParams)]
     lib.b200_layernorm_fwd.restype = ctypes.c_int32
     lib.b200_layernorm_fwd.argtypes = [ctypes.POINTER(LayerNormParams), ctypes.c_void_p]
+    lib.b200_softmax_check.restype = ctypes.c_int32
+    lib.b200_softmax_check.argtypes = [ctypes.POINTER(SoftmaxParams)]
+    lib.b200_softmax_fwd.restype = ctypes.c_int32
+    lib.b200_softmax_fwd.argtypes = [ctypes.POINTER(SoftmaxParams), ctypes.c_void_p]
     return lib
 
 

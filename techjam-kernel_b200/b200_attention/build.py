@@ -1,7 +1,8 @@
 """Build the sm_100a attention library in-tree with nvcc.
 
 The shared library is torch-free: it exports the C ABI declared in
-``include/b200_attn.h``, ``include/b200_linear.h`` and ``include/b200_layernorm.h``
+``include/b200_attn.h``, ``include/b200_linear.h``, ``include/b200_layernorm.h``
+and ``include/b200_softmax.h``
 and links the CUDA runtime statically, so the same file serves the ctypes
 binding here and any other FFI host.
 """
@@ -25,7 +26,7 @@ LIB_PATH = PACKAGE_DIR / LIB_NAME
 # sets B200_ATTN_DEVERR_BOUNDS in the error word instead of faulting).
 CHECKED_LIB_PATH = PACKAGE_DIR / "libb200_attention_checked.so"
 
-SOURCES = ("attn_fwd_sm100.cu", "linear_sm100.cu", "layernorm.cu")
+SOURCES = ("attn_fwd_sm100.cu", "linear_sm100.cu", "layernorm.cu", "softmax.cu")
 HEADERS = ("sm100_ptx.cuh", "error_word.cuh", "byte_range.h")
 
 NVCC_FLAGS = (
@@ -52,7 +53,8 @@ def _nvcc() -> str:
 
 def _inputs() -> list[Path]:
     files = [CSRC / s for s in SOURCES] + [CSRC / h for h in HEADERS]
-    files += [INCLUDE / "b200_attn.h", INCLUDE / "b200_linear.h", INCLUDE / "b200_layernorm.h"]
+    files += [INCLUDE / h for h in ("b200_attn.h", "b200_linear.h", "b200_layernorm.h",
+                                    "b200_softmax.h")]
     return files
 
 

@@ -1,0 +1,343 @@
+// softmax.cu — row softmax over materialised attention scores for B200: the
+// reference's unfused attention seam (model/triton_softmax.py:19-161), whose
+// value is the softmax stage of the organiser's BaselineSelfAttention
+// (torch_transformer_benchmark.py:98-112):
+//   x = round_to_dtype(score * scale); causal / key-mask positions -> -inf;
+//   p = exp(x - max) / sum(exp(x - max)) in fp32 (IEEE division), rounded once.
+//
+// HBM-bound: one read of the scores and one write of the probabilities.  A row
+// is owned by a group of G threads (a warp for rows up to 1024 keys, up to a
+// 1024-thread CTA for 32768 keys) that holds it in registers, EPT elements per
+// thread, loaded with 16-byte vectors when rows are 16-byte aligned; the max
+// and the sum are reduced with warp shuffles (and shared memory across the
+// warps of a group), so every element is read once, exponentiated once and
+// written once.  Rows longer than 32768 keys (up to 65536) run a three-pass
+// form whose re-reads of the row come from L2.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "b200_softmax.h"
+#include "byte_range.h"
+#include "error_word.cuh"
+
+namespace b200sm {
+
+using b200attn::count_launch;
+using b200attn::rows_range;
+using b200attn::set_error;
+
+constexpr int kMaxRegisterRow = 32768;  // longest row held in registers
+constexpr int kLongThreads = 1024;
+
+struct SmArgs {
+  const void* x;
+  void* y;
+  int64_t rows;  // B * H * S
+  int32_t seq;   // S (row length; the query index is row % S)
+  int32_t heads;
+  const uint8_t* mask;
+  int64_t mask_sb, mask_ss;  // bytes
+  float scale;
+  int32_t causal;
+};
+
+// Element type traits: widen to fp32, round an fp32 value to the type.
+template <int DT>
+struct Elem;
+template <>
+struct Elem<B200_ATTN_DTYPE_BF16> {
+  using Raw = uint16_t;
+  __device__ static float widen(Raw v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
+  __device__ static Raw narrow(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+};
+template <>
+struct Elem<B200_ATTN_DTYPE_FP16> {
+  using Raw = uint16_t;
+  __device__ static float widen(Raw v) { return __half2float(__ushort_as_half(v)); }
+  __device__ static Raw narrow(float x) { return __half_as_ushort(__float2half_rn(x)); }
+};
+template <>
+struct Elem<B200_ATTN_DTYPE_FP32> {
+  using Raw = float;
+  __device__ static float widen(Raw v) { return v; }
+  __device__ static Raw narrow(float x) { return x; }
+};
+
+// The score after the scale multiply rounded to the dtype, or -inf when the
+// key is not visible to the row's query.
+template <int DT>
+__device__ __forceinline__ float visible_score(const SmArgs& a, float raw, int64_t col, int64_t q,
+                                               const uint8_t* mrow) {
+  using E = Elem<DT>;
+  bool vis = col < a.seq;
+  if (a.causal) vis = vis && col <= q;
+  if (mrow) vis = vis && col < a.seq && mrow[col * a.mask_ss] != 0;
+  return vis ? E::widen(E::narrow(raw * a.scale)) : -INFINITY;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// G threads per row (32, 128, 512 or 1024), EPT elements per thread.  VEC:
+// rows start on 16-byte boundaries, each thread loads EPT / V vectors of V
+// elements at vector index n * G + t.  Without VEC it loads single elements at
+// n * G + t.  Both are coalesced across the group.
+template <int G, int EPT, int DT, bool VEC>
+__global__ void __launch_bounds__(G < 256 ? 256 : G) softmax_rows_kernel(const SmArgs a) {
+  using E = Elem<DT>;
+  using Raw = typename E::Raw;
+  constexpr int kThreads = G < 256 ? 256 : G;
+  constexpr int kRows = kThreads / G;       // rows per CTA
+  constexpr int kWarps = G / 32;            // warps per row
+  constexpr int V = VEC ? 16 / static_cast<int>(sizeof(Raw)) : 1;
+  constexpr int NV = EPT / V;
+  static_assert(EPT % V == 0, "whole vectors per thread");
+  __shared__ float red[kRows][kWarps > 1 ? kWarps : 1][2];
+
+  const int t = threadIdx.x % G;
+  const int r = threadIdx.x / G;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRows + r;
+  const bool active = row < a.rows;  // inactive threads still join the barriers
+  const int64_t S = a.seq;
+  const int64_t q = active ? row % S : 0;
+  const int64_t b = active ? row / (static_cast<int64_t>(a.heads) * S) : 0;
+  const Raw* xr = static_cast<const Raw*>(a.x) + (active ? row : 0) * S;
+  Raw* yr = static_cast<Raw*>(a.y) + (active ? row : 0) * S;
+  const uint8_t* mrow = a.mask ? a.mask + b * a.mask_sb : nullptr;
+
+  auto col_of = [&](int n, int v) -> int64_t {
+    return VEC ? static_cast<int64_t>(n * G + t) * V + v : static_cast<int64_t>(n * G + t);
+  };
+
+  float x[EPT];
+#pragma unroll
+  for (int n = 0; n < NV; ++n) {
+    const int64_t c0 = col_of(n, 0);
+    if constexpr (VEC) {
+      Raw raw[V];
+      if (active && c0 < S) {
+        *reinterpret_cast<uint4*>(raw) = *reinterpret_cast<const uint4*>(xr + c0);
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; ++v) raw[v] = Raw(0);
+      }
+#pragma unroll
+      for (int v = 0; v < V; ++v) x[n * V + v] = E::widen(raw[v]);
+    } else {
+      x[n] = (active && c0 < S) ? E::widen(xr[c0]) : 0.f;
+    }
+  }
+
+  float m = -INFINITY;
+#pragma unroll
+  for (int n = 0; n < NV; ++n)
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int i = n * V + v;
+      x[i] = active ? visible_score<DT>(a, x[i], col_of(n, v), q, mrow) : -INFINITY;
+      m = fmaxf(m, x[i]);
+    }
+  m = warp_max(m);
+  if constexpr (kWarps > 1) {
+    if ((t & 31) == 0) red[r][t >> 5][0] = m;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, red[r][w][0]);
+  }
+
+  // a row with no visible key keeps m = -inf: x - m is NaN and so is the
+  // row, as torch.softmax of an all -inf row
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < EPT; ++i) {
+    x[i] = expf(x[i] - m);
+    sum += x[i];
+  }
+  sum = warp_sum(sum);
+  if constexpr (kWarps > 1) {
+    if ((t & 31) == 0) red[r][t >> 5][1] = sum;
+    __syncthreads();
+    sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) sum += red[r][w][1];
+  }
+
+  if (!active) return;
+#pragma unroll
+  for (int n = 0; n < NV; ++n) {
+    const int64_t c0 = col_of(n, 0);
+    if (c0 >= S) continue;
+    if constexpr (VEC) {
+      Raw out[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v) out[v] = E::narrow(__fdiv_rn(x[n * V + v], sum));
+      *reinterpret_cast<uint4*>(yr + c0) = *reinterpret_cast<const uint4*>(out);
+    } else {
+      yr[c0] = E::narrow(__fdiv_rn(x[n], sum));
+    }
+  }
+}
+
+// Rows longer than the register form holds: one 1024-thread CTA per row,
+// three passes (max, sum, write) whose second and third reads of the row come
+// from L2 (a row is at most 256 KB and one CTA per SM is resident).
+template <int DT>
+__global__ void __launch_bounds__(kLongThreads) softmax_long_kernel(const SmArgs a) {
+  using E = Elem<DT>;
+  using Raw = typename E::Raw;
+  constexpr int kWarps = kLongThreads / 32;
+  __shared__ float red[kWarps][2];
+  const int64_t row = blockIdx.x;
+  const int t = threadIdx.x;
+  const int64_t S = a.seq;
+  const int64_t q = row % S;
+  const int64_t b = row / (static_cast<int64_t>(a.heads) * S);
+  const Raw* xr = static_cast<const Raw*>(a.x) + row * S;
+  Raw* yr = static_cast<Raw*>(a.y) + row * S;
+  const uint8_t* mrow = a.mask ? a.mask + b * a.mask_sb : nullptr;
+
+  float m = -INFINITY;
+  for (int64_t c = t; c < S; c += kLongThreads)
+    m = fmaxf(m, visible_score<DT>(a, E::widen(xr[c]), c, q, mrow));
+  m = warp_max(m);
+  if ((t & 31) == 0) red[t >> 5][0] = m;
+  __syncthreads();
+  for (int w = 0; w < kWarps; ++w) m = fmaxf(m, red[w][0]);
+
+  float sum = 0.f;
+  for (int64_t c = t; c < S; c += kLongThreads)
+    sum += expf(visible_score<DT>(a, E::widen(xr[c]), c, q, mrow) - m);
+  sum = warp_sum(sum);
+  if ((t & 31) == 0) red[t >> 5][1] = sum;
+  __syncthreads();
+  sum = 0.f;
+  for (int w = 0; w < kWarps; ++w) sum += red[w][1];
+
+  // each thread rewrites only the elements it read, so probs may be scores
+  for (int64_t c = t; c < S; c += kLongThreads) {
+    const float e = expf(visible_score<DT>(a, E::widen(xr[c]), c, q, mrow) - m);
+    yr[c] = E::narrow(__fdiv_rn(e, sum));
+  }
+}
+
+int64_t elem_bytes(int32_t dtype) { return dtype == B200_ATTN_DTYPE_FP32 ? 4 : 2; }
+
+template <int G, int EPT, int DT>
+void launch_rows(const SmArgs& a, bool vec, cudaStream_t s) {
+  constexpr int kRows = (G < 256 ? 256 : G) / G;
+  const unsigned grid = static_cast<unsigned>((a.rows + kRows - 1) / kRows);
+  constexpr int kThreads = G < 256 ? 256 : G;
+  if (vec) softmax_rows_kernel<G, EPT, DT, true><<<grid, kThreads, 0, s>>>(a);
+  else softmax_rows_kernel<G, EPT, DT, false><<<grid, kThreads, 0, s>>>(a);
+}
+
+// Row groups by row length: 8 or 32 elements per thread, G threads per row.
+template <int DT>
+void launch(const SmArgs& a, bool vec, cudaStream_t s) {
+  const int S = a.seq;
+  if (S <= 256) launch_rows<32, 8, DT>(a, vec, s);
+  else if (S <= 1024) launch_rows<32, 32, DT>(a, vec, s);
+  else if (S <= 4096) launch_rows<128, 32, DT>(a, vec, s);
+  else if (S <= 16384) launch_rows<512, 32, DT>(a, vec, s);
+  else if (S <= kMaxRegisterRow) launch_rows<1024, 32, DT>(a, vec, s);
+  else softmax_long_kernel<DT><<<static_cast<unsigned>(a.rows), kLongThreads, 0, s>>>(a);
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace b200sm
+
+using namespace b200sm;
+
+extern "C" int32_t b200_softmax_check(const b200_softmax_params* p) {
+  if (!p || !p->scores || !p->probs) return B200_ATTN_ERR_INVALID_ARGUMENT;
+  if (p->batch < 1 || p->heads < 1 || p->seq_len < 1 || p->seq_len > B200_SOFTMAX_MAX_SEQ)
+    return B200_ATTN_ERR_INVALID_ARGUMENT;
+  // one CTA per row (or per group of rows): rows within the grid limit
+  if (p->batch * p->heads > (1ll << 31) || p->batch * p->heads * p->seq_len > 0x7fffffffll)
+    return B200_ATTN_ERR_INVALID_ARGUMENT;
+  if (!(p->scale > 0.f) || !std::isfinite(p->scale) || p->reserved != 0)
+    return B200_ATTN_ERR_INVALID_ARGUMENT;
+  if (p->dtype != B200_ATTN_DTYPE_BF16 && p->dtype != B200_ATTN_DTYPE_FP16 &&
+      p->dtype != B200_ATTN_DTYPE_FP32)
+    return B200_ATTN_ERR_UNSUPPORTED;
+  const int64_t eb = elem_bytes(p->dtype);
+  if ((reinterpret_cast<uintptr_t>(p->scores) | reinterpret_cast<uintptr_t>(p->probs)) %
+          static_cast<uintptr_t>(eb) != 0)
+    return B200_ATTN_ERR_ALIGNMENT;
+  // probs is scores itself (each group reads its row before writing it) or
+  // disjoint from it
+  const int64_t rows = p->batch * p->heads * p->seq_len;
+  if (p->probs != p->scores &&
+      rows_range(p->probs, rows, p->seq_len, p->seq_len, eb)
+          .overlaps(rows_range(p->scores, rows, p->seq_len, p->seq_len, eb)))
+    return B200_ATTN_ERR_INVALID_ARGUMENT;
+  return B200_ATTN_OK;
+}
+
+extern "C" int32_t b200_softmax_fwd(const b200_softmax_params* p, void* stream) {
+  const int32_t rc = b200_softmax_check(p);
+  if (rc != B200_ATTN_OK) return rc;
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, p->scores) != cudaSuccess || attr.device < 0 ||
+      (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)) {
+    cudaGetLastError();
+    set_error("scores is not a device pointer");
+    return B200_ATTN_ERR_DEVICE;
+  }
+  DeviceGuard guard;
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != attr.device) {
+    if (cudaSetDevice(attr.device) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("cudaSetDevice failed");
+      return B200_ATTN_ERR_DEVICE;
+    }
+    guard.prev = cur;
+  }
+  SmArgs a;
+  a.x = p->scores;
+  a.y = p->probs;
+  a.rows = p->batch * p->heads * p->seq_len;
+  a.seq = static_cast<int32_t>(p->seq_len);
+  a.heads = static_cast<int32_t>(p->heads);
+  a.mask = p->key_mask;
+  a.mask_sb = p->key_mask ? p->mask_stride[0] : 0;
+  a.mask_ss = p->key_mask ? p->mask_stride[1] : 0;
+  a.scale = p->scale;
+  a.causal = p->causal ? 1 : 0;
+  const int64_t eb = elem_bytes(p->dtype);
+  const bool vec = (p->seq_len * eb) % 16 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(p->scores) |
+                     reinterpret_cast<uintptr_t>(p->probs)) & 15u) == 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (p->dtype) {
+    case B200_ATTN_DTYPE_BF16: launch<B200_ATTN_DTYPE_BF16>(a, vec, s); break;
+    case B200_ATTN_DTYPE_FP16: launch<B200_ATTN_DTYPE_FP16>(a, vec, s); break;
+    default: launch<B200_ATTN_DTYPE_FP32>(a, vec, s); break;
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(cudaGetErrorString(e));
+    return B200_ATTN_ERR_LAUNCH;
+  }
+  count_launch();
+  return B200_ATTN_OK;
+}
