@@ -56,6 +56,10 @@ WORKLOADS = {
     # global batch 8 split over the ranks (data parallel)
     "cfg5": dict(B=8, H=16, S=2048, D=64, causal=True, masked=False, shard="batch_split",
                  layers=12, d_model=1024, ffn=4096, vocab=32000),
+    # the row softmax over materialised scores (the reference's unfused seam,
+    # model/triton_softmax.py) at cfg2's score shape [8, 16, 2048, 2048]
+    "sm2": dict(B=8, H=16, S=2048, D=128, causal=True, masked=False, shard="batch",
+                kind="softmax"),
     # the reference's only published attention timing (fp16 two-pass tiled
     # attention, docs/TECH_REPORT.md:98-111): 0.590592 ms on an RTX 5070 Ti
     "tr": dict(B=64, H=4, S=1024, D=32, causal=True, masked=False, shard="batch", dtype="float16",
@@ -398,6 +402,125 @@ def run_dense_arm(args, cfg: dict, rank: int, world: int) -> int:
     return 0
 
 
+def run_softmax_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, barrier,
+                    max_over_ranks) -> int:
+    """The row softmax over materialised [B, H, S, S] scores (HBM-bound): value
+    = whole-job GB/s of algorithmic bytes (scores read once, probabilities
+    written once); inputs rotate over buffers larger than L2."""
+    import torch
+    import torch.distributed as dist
+
+    from b200_attention import _native
+    from b200_attention.fused_attention import read_device_errors
+    from b200_attention.softmax import b200_attention_softmax
+    from oracle.reference_attention import reference_softmax
+
+    B, H, scaling = shard_for(cfg, world, rank)
+    S, D, causal = cfg["S"], cfg["D"], cfg["causal"]
+    dtype = cfg_dtype(cfg)
+    elem = torch.finfo(dtype).bits // 8
+    nbytes = 2.0 * B * H * S * S * elem
+    n_sets = max(2, math.ceil(2 * L2_BYTES / (B * H * S * S * elem)))
+    gen = torch.Generator(device=dev).manual_seed(args.seed + 1000 * rank)
+    scores = [(4 * torch.randn((B, H, S, S), generator=gen, device=dev)).to(dtype)
+              for _ in range(n_sets)]
+    outs = [torch.empty_like(t) for t in scores]
+
+    def step(i):
+        return b200_attention_softmax(scores[i % n_sets], None, D ** -0.5, causal,
+                                      out=outs[i % n_sets])
+
+    stream = torch.cuda.current_stream(dev)
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if read_device_errors(dev):
+        raise RuntimeError("kernel reported a device error during warm-up")
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    sampler = ClockSampler(local_rank)
+    barrier()
+    torch.cuda.synchronize(dev)
+    launches0 = _native.launch_count()
+    with sampler:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            step(i)
+            ev[i][1].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    launches = _native.launch_count() - launches0
+    ms_per_step = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    value = world * nbytes / (ms_per_step * 1e-3) / 1e9
+
+    # end to end: scores up from pinned host memory and probabilities back,
+    # every step, through the public operator
+    hs = scores[0].cpu().pin_memory()
+    ho = torch.empty_like(hs).pin_memory()
+    e2e_steps = args.e2e_steps or 3
+    d_in, d_out = torch.empty_like(scores[0]), torch.empty_like(scores[0])
+    torch.cuda.synchronize(dev)
+    barrier()
+    t0.record(stream)
+    for _ in range(e2e_steps):
+        d_in.copy_(hs, non_blocking=True)
+        b200_attention_softmax(d_in, None, D ** -0.5, causal, out=d_out)
+        ho.copy_(d_out, non_blocking=True)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1)) / e2e_steps
+    if not torch.equal(ho, outs[0].cpu()):
+        raise RuntimeError("end-to-end softmax differs from the device-resident run")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        heads = max(1, min(H, int(2 ** 31 // (S * S * 12))))
+        hs1 = scores[0][:1, :heads].cpu()
+        times = []
+        while sum(times) < args.cpu_budget or len(times) < 3:
+            c0 = time.perf_counter()
+            reference_softmax(hs1, None, D ** -0.5, causal)
+            times.append(time.perf_counter() - c0)
+        med = statistics.median(times)
+        sample_bytes = 2.0 * heads * S * S * elem
+        cpu = {"value": sample_bytes / med / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+               "kind": "port", "ms_per_step_extrapolated": nbytes / (sample_bytes / med) * 1e3,
+               "sample": f"{len(times)} reps of oracle.reference_softmax (torch CPU, reference op "
+                         f"order) on [1,{heads},{S},{S}]"}
+    peaks, peak_src = load_peaks()
+    gbs = nbytes / (launch_ms * 1e-3) / 1e9
+    roof = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": gbs / peaks["hbm_gbs"], "traffic": None, "algorithmic_bytes": nbytes,
+            "avg_launch_ms": launch_ms, "peak_source": f"{peak_src} hbm_gbs",
+            "kernel": "softmax_rows_kernel"}
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": "row softmax over materialised attention scores, GB/s", "value": value,
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": scaling,
+        "vs_baseline": None, "dtype": dtype_tag(cfg), "data": "synthetic (seeded 4 * N(0,1) scores)",
+        "config": {"workload": args.workload, "B": B, "H": H, "S": S, "causal": causal,
+                   "l2": f"{n_sets} score buffers of {B * H * S * S * elem / 2**20:.0f} MiB (> L2)"},
+        "roofline": roof, "cpu_baseline": cpu,
+        "e2e": {"value": world * nbytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": hs.numel() * elem, "d2h_bytes_per_step": ho.numel() * elem,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": launches, "clocks": sampler.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, barrier,
                   max_over_ranks) -> int:
     """cfg5: forward of the 12-layer decoder whose attention is the sm_100a kernel.
@@ -643,6 +766,8 @@ def main(argv=None) -> int:
 
     if args.workload == "cfg5":
         return run_model_arm(args, cfg, rank, world, local_rank, dev, barrier, max_over_ranks)
+    if cfg.get("kind") == "softmax":
+        return run_softmax_arm(args, cfg, rank, world, local_rank, dev, barrier, max_over_ranks)
 
     B, H, scaling = shard_for(cfg, world, rank)
     S, D, causal = cfg["S"], cfg["D"], cfg["causal"]

@@ -87,8 +87,54 @@ def build_native(force: bool = False, verbose: bool = False, checked: bool = Fal
     return out
 
 
+# The attention operator as a torch custom op (torch.ops.b200.fused_attention)
+# over the same C ABI: a C++ translation unit against torch's headers, linked
+# to libb200_attention.so found next to it ($ORIGIN).
+TORCH_OP_SOURCE = CSRC / "torch_op.cpp"
+TORCH_OP_PATH = PACKAGE_DIR / "libb200_attention_torch.so"
+
+
+def _torch_op_stale() -> bool:
+    if not TORCH_OP_PATH.exists():
+        return True
+    built = TORCH_OP_PATH.stat().st_mtime
+    deps = (TORCH_OP_SOURCE, INCLUDE / "b200_attn.h", LIB_PATH)
+    return any(f.stat().st_mtime > built for f in deps if f.exists())
+
+
+def build_torch_op(force: bool = False, verbose: bool = False) -> Path:
+    """Compile ``libb200_attention_torch.so`` (needs the C-ABI library built
+    first); skipped when fresh."""
+    if not force and not _torch_op_stale():
+        return TORCH_OP_PATH
+    import torch
+    from torch.utils import cpp_extension
+
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH.name} must be built before the torch op")
+    includes = cpp_extension.include_paths(device_type="cuda") + [str(INCLUDE)]
+    libdirs = cpp_extension.library_paths(device_type="cuda")
+    torch_lib = str(Path(torch.__file__).resolve().parent / "lib")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = TORCH_OP_PATH.with_suffix(".so.tmp")
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           *[f"-I{d}" for d in includes], str(TORCH_OP_SOURCE),
+           *[f"-L{d}" for d in libdirs], f"-L{PACKAGE_DIR}",
+           "-l:libb200_attention.so", "-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}", "-o", str(tmp)]
+    if verbose:
+        print(" ".join(cmd))
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"g++ failed ({proc.returncode}):\n{proc.stderr[-8000:]}")
+    os.replace(tmp, TORCH_OP_PATH)
+    return TORCH_OP_PATH
+
+
 if __name__ == "__main__":
     import sys
 
     print(build_native(force="--force" in sys.argv, verbose="-v" in sys.argv))
     print(build_native(force="--force" in sys.argv, checked=True))
+    print(build_torch_op(force="--force" in sys.argv, verbose="-v" in sys.argv))

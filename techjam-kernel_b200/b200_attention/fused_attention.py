@@ -9,6 +9,10 @@ consumed through their strides), ``valid_token_mask`` is an optional bool
 ``D ** -0.5`` and must be positive, and ``output_bshd`` selects a contiguous
 ``[B, S, H, D]`` output instead of ``[B, H, S, D]``.
 
+The call is one torch custom op over the C ABI (``csrc/torch_op.cpp``);
+``make_params`` packs the same C struct for callers that use the C ABI
+directly (the self-test and bounds-checked entry points).
+
 One deliberate difference: the reference silently falls back to dense PyTorch
 for inputs its kernels do not cover (:1906-1925).  This operator has no fallback
 of any kind; inputs outside the kernel envelope raise ``ValueError`` whatever
@@ -233,6 +237,37 @@ def make_params(
     return p
 
 
+_op = None
+_op_lock = threading.Lock()
+_word_ptrs: dict = {}
+
+
+def _attention_op():
+    """torch.ops.b200.fused_attention, loaded once from this directory.  Raises
+    when the library has not been built; there is no other implementation."""
+    global _op
+    if _op is None:
+        with _op_lock:
+            if _op is None:
+                from .build import TORCH_OP_PATH
+
+                if not TORCH_OP_PATH.exists():
+                    raise RuntimeError(f"{TORCH_OP_PATH.name} is not built; run "
+                                       "`python -m b200_attention.build` or __graft_entry__.build()")
+                _native.load_library()
+                torch.ops.load_library(str(TORCH_OP_PATH))
+                _op = torch.ops.b200.fused_attention
+    return _op
+
+
+def _error_word_address(device: torch.device) -> int:
+    address = _word_ptrs.get(device)
+    if address is None:
+        address = _word_ptrs[device] = (device_error_word(device).data_ptr()
+                                        if device.type == "cuda" else 0)
+    return address
+
+
 def b200_fused_attention(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -259,48 +294,25 @@ def b200_fused_attention(
     query blocks that lie entirely past the last valid key.  ``out`` may supply
     the output tensor (same shape/dtype/device, contiguous last dim).
 
-    ``block_m``/``block_n`` are accepted for signature compatibility; the kernel
-    uses fixed 128 x 128 tiles and rejects other values.  ``num_warps`` and
-    ``num_stages`` are accepted and ignored (the kernel's warp roles and ring
-    depth are fixed per head dimension).  ``strict`` is accepted; unsupported
-    inputs always raise.
+    The call is one torch custom op (``torch.ops.b200.fused_attention``,
+    ``csrc/torch_op.cpp``) over the C ABI: the reference's input checks with
+    its exception types, the output allocation and the launch on the current
+    stream happen in C++.  ``block_m``/``block_n`` are accepted for signature
+    compatibility; the kernel uses fixed 128 x 128 tiles and rejects other
+    values.  ``num_warps`` and ``num_stages`` are accepted and ignored (the
+    kernel's warp roles and ring depth are fixed per head dimension).
+    ``strict`` is accepted; unsupported inputs always raise.
     """
-    batch, heads, seq_len, head_dim = _validate_inputs(q, k, v, valid_token_mask)
-    if scale is None:
-        scale = head_dim**-0.5
-    if scale <= 0.0:
-        raise ValueError("scale must be positive")
     if block_m not in (None, BLOCK_M) or block_n not in (None, BLOCK_N):
         raise ValueError(f"the sm_100a kernel uses {BLOCK_M}x{BLOCK_N} tiles")
-    reason = unsupported_reason(q, k, v)
-    if reason is not None:
-        raise ValueError(f"unsupported sm_100a attention invocation: {reason}")
-    if zero_masked_queries and valid_token_mask is None:
-        raise ValueError("zero_masked_queries requires valid_token_mask")
-    if output_bshd:
-        shape = (batch, seq_len, heads, head_dim)
-        if out is None:
-            out = torch.empty(shape, device=q.device, dtype=q.dtype)
-        elif tuple(out.shape) != shape:
-            raise ValueError(f"out must have shape {shape}")
-        out_bhsd = out.transpose(1, 2)
-    else:
-        shape = (batch, heads, seq_len, head_dim)
-        if out is None:
-            out = torch.empty(shape, device=q.device, dtype=q.dtype)
-        elif tuple(out.shape) != shape:
-            raise ValueError(f"out must have shape {shape}")
-        out_bhsd = out
-    if out.dtype != q.dtype or out.device != q.device or out_bhsd.stride(-1) != 1:
-        raise ValueError("out must match q's dtype and device with a contiguous last dim")
-
-    lib = _native.load_library()
-    params = make_params(
-        q, k, v, out_bhsd, valid_token_mask, causal, scale, zero_masked_queries,
-        device_error_word(q.device),
-    )
-    stream = torch.cuda.current_stream(q.device).cuda_stream
-    rc = lib.b200_attn_fwd(ctypes.byref(params), ctypes.c_void_p(stream))
-    if rc != _native.OK:
-        raise_for_code("b200_attn_fwd", rc, q.device)
-    return out
+    op = _op if _op is not None else _attention_op()
+    try:
+        return op(q, k, v, valid_token_mask, causal, scale, output_bshd, zero_masked_queries, out,
+                  _error_word_address(q.device))
+    except RuntimeError as exc:
+        if str(exc).startswith("b200 device error"):
+            value = int(device_error_word(q.device)[0])
+            raise DeviceError(f"b200_attn_fwd refused to launch: an earlier kernel on {q.device} "
+                              f"reported a {_describe(value)}; its output is undefined "
+                              "(clear_device_errors resumes launches)") from None
+        raise

@@ -90,20 +90,60 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Packed fp32 pairs (sm_100 .f32x2): each lane rounds like the scalar op.
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+// 2^x on the MUFU; subnormal results are kept (bf16 probabilities share
+// fp32's exponent range)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// A pair of scores after the scale multiply, rounded to the dtype.
+template <int DT>
+__device__ __forceinline__ float2 scaled_pair(float2 x, float scale) {
+  using E = Elem<DT>;
+  const float2 s = mul2(x, make_float2(scale, scale));
+  return make_float2(E::widen(E::narrow(s.x)), E::widen(E::narrow(s.y)));
+}
+
 // G threads per row (32, 128, 512 or 1024), EPT elements per thread.  VEC:
 // rows start on 16-byte boundaries, each thread loads EPT / V vectors of V
 // elements at vector index n * G + t.  Without VEC it loads single elements at
 // n * G + t.  Both are coalesced across the group.
+//
+// 16-bit outputs take exp(x - m) as ex2(x * log2e - m * log2e) (one FMA and
+// one MUFU operation; the argument's fp32 rounding changes the result by a
+// few fp32 units, far below the 16-bit rounding) and multiply by the row sum's
+// reciprocal; fp32 outputs keep expf and an IEEE division per element.
 template <int G, int EPT, int DT, bool VEC>
 __global__ void __launch_bounds__(G < 256 ? 256 : G) softmax_rows_kernel(const SmArgs a) {
   using E = Elem<DT>;
   using Raw = typename E::Raw;
+  constexpr bool kExact = DT == B200_ATTN_DTYPE_FP32;
+  constexpr float kLog2e = 1.4426950408889634f;
   constexpr int kThreads = G < 256 ? 256 : G;
   constexpr int kRows = kThreads / G;       // rows per CTA
   constexpr int kWarps = G / 32;            // warps per row
   constexpr int V = VEC ? 16 / static_cast<int>(sizeof(Raw)) : 1;
   constexpr int NV = EPT / V;
-  static_assert(EPT % V == 0, "whole vectors per thread");
+  static_assert(EPT % V == 0 && EPT % 2 == 0, "whole vectors and pairs per thread");
   __shared__ float red[kRows][kWarps > 1 ? kWarps : 1][2];
 
   const int t = threadIdx.x % G;
@@ -116,6 +156,9 @@ __global__ void __launch_bounds__(G < 256 ? 256 : G) softmax_rows_kernel(const S
   const Raw* xr = static_cast<const Raw*>(a.x) + (active ? row : 0) * S;
   Raw* yr = static_cast<Raw*>(a.y) + (active ? row : 0) * S;
   const uint8_t* mrow = a.mask ? a.mask + b * a.mask_sb : nullptr;
+  // V mask bytes in one load: a byte-contiguous, V-aligned mask row
+  const bool mask_vec = VEC && mrow && a.mask_ss == 1 &&
+                        (reinterpret_cast<uintptr_t>(mrow) & (V - 1)) == 0;
 
   auto col_of = [&](int n, int v) -> int64_t {
     return VEC ? static_cast<int64_t>(n * G + t) * V + v : static_cast<int64_t>(n * G + t);
@@ -141,14 +184,52 @@ __global__ void __launch_bounds__(G < 256 ? 256 : G) softmax_rows_kernel(const S
   }
 
   float m = -INFINITY;
+  if constexpr (VEC) {
 #pragma unroll
-  for (int n = 0; n < NV; ++n)
+    for (int n = 0; n < NV; ++n) {
+      const int64_t c0 = col_of(n, 0);
+      float* xv = x + n * V;
 #pragma unroll
-    for (int v = 0; v < V; ++v) {
-      const int i = n * V + v;
-      x[i] = active ? visible_score<DT>(a, x[i], col_of(n, v), q, mrow) : -INFINITY;
+      for (int v = 0; v < V; v += 2) {
+        const float2 sp = scaled_pair<DT>(make_float2(xv[v], xv[v + 1]), a.scale);
+        xv[v] = sp.x;
+        xv[v + 1] = sp.y;
+      }
+      // the whole vector is in the row (S is a multiple of V); causality and
+      // the mask are tested only where they can hide a key
+      if (!active || c0 >= S) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) xv[v] = -INFINITY;
+      } else {
+        if (a.causal && c0 + V - 1 > q) {
+#pragma unroll
+          for (int v = 0; v < V; ++v)
+            if (c0 + v > q) xv[v] = -INFINITY;
+        }
+        if (mrow) {
+          uint8_t mb[V];
+          if (mask_vec) {
+            if constexpr (V == 8) *reinterpret_cast<uint2*>(mb) = *reinterpret_cast<const uint2*>(mrow + c0);
+            else *reinterpret_cast<uint32_t*>(mb) = *reinterpret_cast<const uint32_t*>(mrow + c0);
+          } else {
+#pragma unroll
+            for (int v = 0; v < V; ++v) mb[v] = mrow[(c0 + v) * a.mask_ss];
+          }
+#pragma unroll
+          for (int v = 0; v < V; ++v)
+            if (!mb[v]) xv[v] = -INFINITY;
+        }
+      }
+#pragma unroll
+      for (int v = 0; v < V; ++v) m = fmaxf(m, xv[v]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      x[i] = active ? visible_score<DT>(a, x[i], col_of(i, 0), q, mrow) : -INFINITY;
       m = fmaxf(m, x[i]);
     }
+  }
   m = warp_max(m);
   if constexpr (kWarps > 1) {
     if ((t & 31) == 0) red[r][t >> 5][0] = m;
@@ -160,10 +241,25 @@ __global__ void __launch_bounds__(G < 256 ? 256 : G) softmax_rows_kernel(const S
   // a row with no visible key keeps m = -inf: x - m is NaN and so is the
   // row, as torch.softmax of an all -inf row
   float sum = 0.f;
+  if constexpr (kExact) {
 #pragma unroll
-  for (int i = 0; i < EPT; ++i) {
-    x[i] = expf(x[i] - m);
-    sum += x[i];
+    for (int i = 0; i < EPT; ++i) {
+      x[i] = expf(x[i] - m);
+      sum += x[i];
+    }
+  } else {
+    const float2 l2 = make_float2(kLog2e, kLog2e);
+    const float2 nm = make_float2(-m * kLog2e, -m * kLog2e);
+    float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < EPT; i += 2) {
+      const float2 arg = fma2(make_float2(x[i], x[i + 1]), l2, nm);
+      x[i] = ex2_approx(arg.x);
+      x[i + 1] = ex2_approx(arg.y);
+      s2.x += x[i];
+      s2.y += x[i + 1];
+    }
+    sum = s2.x + s2.y;
   }
   sum = warp_sum(sum);
   if constexpr (kWarps > 1) {
@@ -175,6 +271,7 @@ __global__ void __launch_bounds__(G < 256 ? 256 : G) softmax_rows_kernel(const S
   }
 
   if (!active) return;
+  const float inv = kExact ? 0.f : __frcp_rn(sum);
 #pragma unroll
   for (int n = 0; n < NV; ++n) {
     const int64_t c0 = col_of(n, 0);
@@ -182,10 +279,19 @@ __global__ void __launch_bounds__(G < 256 ? 256 : G) softmax_rows_kernel(const S
     if constexpr (VEC) {
       Raw out[V];
 #pragma unroll
-      for (int v = 0; v < V; ++v) out[v] = E::narrow(__fdiv_rn(x[n * V + v], sum));
+      for (int v = 0; v < V; v += 2) {
+        if constexpr (kExact) {
+          out[v] = E::narrow(__fdiv_rn(x[n * V + v], sum));
+          out[v + 1] = E::narrow(__fdiv_rn(x[n * V + v + 1], sum));
+        } else {
+          const float2 pv = mul2(make_float2(x[n * V + v], x[n * V + v + 1]), make_float2(inv, inv));
+          out[v] = E::narrow(pv.x);
+          out[v + 1] = E::narrow(pv.y);
+        }
+      }
       *reinterpret_cast<uint4*>(yr + c0) = *reinterpret_cast<const uint4*>(out);
     } else {
-      yr[c0] = E::narrow(__fdiv_rn(x[n], sum));
+      yr[c0] = E::narrow(kExact ? __fdiv_rn(x[n], sum) : x[n] * inv);
     }
   }
 }

@@ -90,3 +90,27 @@ def test_error_word_survives_inference_mode(monkeypatch):
     monkeypatch.undo()
     assert not word.is_inference()
     word.zero_()
+
+
+def test_operator_is_a_torch_custom_op_with_the_reference_exception_types():
+    """The operator is torch.ops.b200.fused_attention (C++ over the C ABI): the
+    reference's ValueError / TypeError contract holds through the dispatcher."""
+    from b200_attention.fused_attention import _attention_op
+
+    op = _attention_op()
+    assert op is torch.ops.b200.fused_attention
+    schema = str(op.default._schema)
+    assert "Tensor? valid_token_mask" in schema and "int error_word" in schema
+    q = torch.randn(1, 2, 8, 64).bfloat16()
+    with pytest.raises(ValueError, match="same \\[B, H, S, D\\] shape"):
+        op(q, q[:, :1], q, None, False, None, False, False, None, 0)
+    with pytest.raises(TypeError, match="same dtype"):
+        op(q, q.half(), q, None, False, None, False, False, None, 0)
+    with pytest.raises(TypeError, match="floating-point"):
+        op(q.int(), q.int(), q.int(), None, False, None, False, False, None, 0)
+    with pytest.raises(TypeError, match="torch.bool"):
+        op(q, q, q, torch.ones(1, 8), False, None, False, False, None, 0)
+    with pytest.raises(ValueError, match="scale must be positive"):
+        op(q, q, q, None, False, 0.0, False, False, None, 0)
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        op(q, q, q, None, False, None, False, False, None, 0)
