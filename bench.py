@@ -722,6 +722,9 @@ def main(argv=None) -> int:
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--graph", action="store_true",
                     help="replay the timed steps from a CUDA graph (launch-bound workloads)")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="override the workload's head count (smaller cases for profiler "
+                         "captures; the line's config records it)")
     ap.add_argument("--unfused-epilogues", action="store_true",
                     help="cfg5: run the block's linear layers on cuBLAS with separate GELU/add "
                          "passes (the yardstick for the fused linear kernel)")
@@ -729,7 +732,9 @@ def main(argv=None) -> int:
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
 
-    cfg = WORKLOADS[args.workload]
+    cfg = dict(WORKLOADS[args.workload])
+    if args.heads is not None:
+        cfg["H"] = args.heads
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
