@@ -56,6 +56,10 @@ WORKLOADS = {
     # global batch 8 split over the ranks (data parallel)
     "cfg5": dict(B=8, H=16, S=2048, D=64, causal=True, masked=False, shard="batch_split",
                  layers=12, d_model=1024, ffn=4096, vocab=32000),
+    # context parallelism: one long causal sequence sharded (zigzag) over the
+    # ranks, K/V passed around a ring; strong scaling
+    "cp": dict(B=1, H=8, S=131072, D=128, causal=True, masked=False, shard="sequence",
+               kind="context_parallel"),
     # the row softmax over materialised scores (the reference's unfused seam,
     # model/triton_softmax.py) at cfg2's score shape [8, 16, 2048, 2048]
     "sm2": dict(B=8, H=16, S=2048, D=128, causal=True, masked=False, shard="batch",
@@ -521,6 +525,92 @@ def run_softmax_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev
     return 0
 
 
+def run_context_parallel_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev,
+                             barrier, max_over_ranks) -> int:
+    """One long causal sequence sharded over the ranks in zigzag order, K/V
+    passed around a ring (NCCL send/recv) while the kernel's partial form
+    attends to the chunk at hand.  value = whole-sequence attention TFLOP/s
+    (4 B H S^2 D / 2) over the max-over-ranks time; N = 1 runs the same chunk
+    pairs on one GPU."""
+    import torch
+    import torch.distributed as dist
+
+    from b200_attention import _native
+    from b200_attention.context_parallel import (b200_partial_attention, ring_attention,
+                                                 shard_sequence)
+    from b200_attention.fused_attention import b200_fused_attention, read_device_errors
+
+    B, H, S, D = cfg["B"], cfg["H"], cfg["S"], cfg["D"]
+    dtype = cfg_dtype(cfg)
+    flop = 4.0 * B * H * S * S * D / 2
+    gen = torch.Generator(device="cpu").manual_seed(args.seed)
+    q, k, v = (torch.randn((B, H, S, D), generator=gen).to(dtype) for _ in range(3))
+    shares = [shard_sequence(t, world, rank).to(dev) for t in (q, k, v)]
+    scale = D ** -0.5
+
+    def step():
+        return ring_attention(*shares, True, scale, b200_partial_attention)[0]
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    if read_device_errors(dev):
+        raise RuntimeError("kernel reported a device error during warm-up")
+    sampler = ClockSampler(local_rank)
+    barrier()
+    torch.cuda.synchronize(dev)
+    launches0 = _native.launch_count()
+    with sampler:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            out = step()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    launches = _native.launch_count() - launches0
+    ms_per_step = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+    value = flop / (ms_per_step * 1e-3) / 1e12
+    finite = bool(torch.isfinite(out.float()).all())
+    single = None
+    if world == 1:
+        # the same sequence in one plain launch, for the cost of the chunking
+        qd, kd, vd = (t.to(dev) for t in (q, k, v))
+        b200_fused_attention(qd, kd, vd, None, True)
+        torch.cuda.synchronize(dev)
+        t0.record(stream)
+        for _ in range(3):
+            b200_fused_attention(qd, kd, vd, None, True)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        single = flop / (t0.elapsed_time(t1) / 3 * 1e-3) / 1e12
+    peaks, peak_src = load_peaks()
+    per_gpu = value / world
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": dtype_tag(cfg),
+        "data": "synthetic (seeded torch.randn N(0,1))",
+        "config": {"workload": args.workload, "B": B, "H": H, "S": S, "D": D, "causal": True,
+                   "parallelism": f"context-parallel x{world}: zigzag sequence shards, K/V ring "
+                                  "over NCCL send/recv overlapped with the partial kernel",
+                   "chunk_len": S // (2 * world)},
+        "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": per_gpu / peaks["bf16_tflops"], "traffic": None,
+                     "peak_source": f"{peak_src} bf16_tflops", "per": "GPU (whole-step average)"},
+        "single_launch_tflops": single, "gpu_launches": launches, "clocks": sampler.summary(),
+        "validation": {"finite": finite},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_model_arm(args, cfg: dict, rank: int, world: int, local_rank: int, dev, barrier,
                   max_over_ranks) -> int:
     """cfg5: forward of the 12-layer decoder whose attention is the sm_100a kernel.
@@ -773,6 +863,9 @@ def main(argv=None) -> int:
         return run_model_arm(args, cfg, rank, world, local_rank, dev, barrier, max_over_ranks)
     if cfg.get("kind") == "softmax":
         return run_softmax_arm(args, cfg, rank, world, local_rank, dev, barrier, max_over_ranks)
+    if cfg.get("kind") == "context_parallel":
+        return run_context_parallel_arm(args, cfg, rank, world, local_rank, dev, barrier,
+                                        max_over_ranks)
 
     B, H, scaling = shard_for(cfg, world, rank)
     S, D, causal = cfg["S"], cfg["D"], cfg["causal"]

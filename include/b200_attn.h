@@ -164,6 +164,32 @@ B200_ATTN_API int32_t b200_attn_launch_shape(int32_t dtype, int64_t head_dim, in
                                              int32_t* rows_per_cta, int32_t* block_n,
                                              int32_t* num_warps, int32_t* ring_slots);
 
+/* One step of context-parallel attention (no reference counterpart: the
+ * reference runs every sequence on one device).  A sequence too long for one
+ * GPU is split into chunks of equal length; the query chunk attends to one key
+ * chunk per call, and the calls for all key chunks the query chunk sees are
+ * merged in the output, exactly as attention over the whole key sequence:
+ *   lse[b, h, i] = log(sum_j exp(scores[i, j]))      (this chunk's visible keys)
+ *   accumulate = 0:  O = softmax over this chunk (as b200_attn_fwd),  lse written
+ *   accumulate = 1:  O, lse = the merge of the (O, lse) in memory with this chunk's:
+ *                    lse' = log(exp(lse) + exp(lse_chunk)),
+ *                    O'   = O * exp(lse - lse') + O_chunk * exp(lse_chunk - lse')
+ * `base.causal` is the diagonal chunk's mask (key j visible to query i iff
+ * j <= i inside the chunk pair); a key chunk wholly before the query chunk is
+ * passed with causal = 0 and one wholly after it is not passed.  A row that saw
+ * no visible key in any chunk is NaN with lse -inf.  Key masks and
+ * zero_masked_queries are not taken (B200_ATTN_ERR_UNSUPPORTED).  O is read
+ * and written in the element type, so each accumulating call rounds it once. */
+typedef struct b200_attn_partial_params {
+  b200_attn_fwd_params base;
+  float* lse;              /* [B, H, S] fp32 log-sum-exp (natural log), read when accumulating */
+  int64_t lse_stride[3];   /* {batch, head, seq} in elements */
+  int32_t accumulate;      /* 0: first chunk; 1: merge into (base.o, lse) */
+  int32_t reserved;        /* 0 */
+} b200_attn_partial_params;
+
+B200_ATTN_API int32_t b200_attn_fwd_partial(const b200_attn_partial_params* p, void* stream);
+
 /* Self-test of failure detection (no reference counterpart).  Launches the
  * forward exactly like b200_attn_fwd, except that in every CTA the K/V load
  * number `skipped_load` (0 = first K tile, 1 = first V tile, ...) is announced

@@ -45,6 +45,7 @@ EXPORTED_SYMBOLS = (
     "b200_attn_selftest_stall",
     "b200_attn_launch_count",
     "b200_attn_launch_shape",
+    "b200_attn_fwd_partial",
 )
 # Every symbol ``include/b200_linear.h`` declares.
 LINEAR_SYMBOLS = (
@@ -95,6 +96,18 @@ class FwdParams(ctypes.Structure):
         ("causal", ctypes.c_int32),
         ("zero_masked_queries", ctypes.c_int32),
         ("error_word", ctypes.c_void_p),
+    ]
+
+
+class PartialParams(ctypes.Structure):
+    """Mirror of ``b200_attn_partial_params``."""
+
+    _fields_ = [
+        ("base", FwdParams),
+        ("lse", ctypes.c_void_p),
+        ("lse_stride", ctypes.c_int64 * 3),
+        ("accumulate", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -187,6 +200,8 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.b200_attn_launch_shape.restype = ctypes.c_int32
     lib.b200_attn_launch_shape.argtypes = [ctypes.c_int32, ctypes.c_int64] + [
         ctypes.POINTER(ctypes.c_int32)] * 5
+    lib.b200_attn_fwd_partial.restype = ctypes.c_int32
+    lib.b200_attn_fwd_partial.argtypes = [ctypes.POINTER(PartialParams), ctypes.c_void_p]
     lib.b200_attn_selftest_stall.restype = ctypes.c_int32
     lib.b200_attn_selftest_stall.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_int32,
                                              ctypes.c_void_p]

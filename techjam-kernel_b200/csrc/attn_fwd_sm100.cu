@@ -122,6 +122,25 @@ struct KernelArgs {
   int32_t skip_load;     // stall self-test only: K/V load left out (see b200_attn_selftest_stall)
 };
 
+// Arguments of the partial instances (b200_attn_fwd_partial): the per-row
+// log-sum-exp of this key chunk, merged into the existing (O, lse) when
+// accumulate is set.  A separate type, so the other instances' arguments
+// (and their code) are unchanged.
+struct PartialKernelArgs : KernelArgs {
+  float* lse;
+  int64_t lse_sb, lse_sh, lse_ss;  // elements
+  int32_t accumulate;
+};
+
+template <bool kPartial>
+struct ArgsOf {
+  using type = KernelArgs;
+};
+template <>
+struct ArgsOf<true> {
+  using type = PartialKernelArgs;
+};
+
 // Compile-time shape of one kernel instance.  ELEM is the element size: 2
 // for bf16/fp16 (kind::f16 products), 4 for fp32 (kind::tf32 products).
 template <int D_, int BN_, int PB_, int NSLOT_, bool SHARED_S_, int ELEM_ = 2>
@@ -379,17 +398,24 @@ __device__ __forceinline__ void mask_row(uint32_t (&s)[N], int lim, const uint32
 // kStallProbe (self-test instance only): K/V load number args.skip_load of
 // every CTA is announced to its barrier but never issued, so the pipeline
 // waits on it run out and exercise the abort path.
-template <class C, bool kCausal, bool kMask, int kDtype, bool kStallProbe = false>
+// kPartial (b200_attn_fwd_partial): the CTA also writes each row's
+// log-sum-exp over this key chunk and, with args.accumulate, merges its
+// normalised output into the O and lse already in memory (the context-parallel
+// step over one chunk of a longer key sequence).
+template <class C, bool kCausal, bool kMask, int kDtype, bool kStallProbe = false,
+          bool kPartial = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v,
-                          const __grid_constant__ CUtensorMap tm_o, const KernelArgs args) {
+                          const __grid_constant__ CUtensorMap tm_o,
+                          const typename ArgsOf<kPartial>::type args) {
   constexpr int D = C::D, BN = C::BN, PB = C::PB, NSLOT = C::NSLOT;
   constexpr int kMaskWords = BN / 32;
   constexpr bool kBF16 = kDtype == B200_ATTN_DTYPE_BF16;
   constexpr bool kTF32 = kDtype == B200_ATTN_DTYPE_FP32;  // fp32 inputs, TF32 products
   static_assert(kTF32 == (C::ELEM == 4), "fp32 runs the 32-bit instance");
+  static_assert(!(kPartial && kMask), "partial instances take no key mask");
   constexpr int kCC = C::kChunkCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -729,6 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     float m_run = -INFINITY;
     float l_run = 0.f;
+    float lse_row = -INFINITY;  // partial instances: natural-log log-sum-exp of the row
     bool ok = true;
 
     if (n <= C::kExactTiles) {
@@ -810,6 +837,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         m_run = mx;   // -inf only when the row has no visible key (NaN output)
         l_run = 1.f;  // P is already normalised
+        if constexpr (kPartial) lse_row = (mx == -INFINITY) ? -INFINITY : sub + logf(tot);
       }
     } else {
       for (int j = 0; j < n; ++j) {
@@ -937,6 +965,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tmem_wait_st();
         warp_arrive(bar_p_full(j), lane);
       }
+      if constexpr (kPartial)
+        lse_row = (m_run == -INFINITY) ? -INFINITY
+                                       : (m_run + log2f(l_run)) * 0.6931471805599453f;
     }
 
     // ------------------------------------------------------------ epilogue
@@ -961,6 +992,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv_l =
           zero_row ? 0.f : (m_run == -INFINITY ? __int_as_float(0x7fc00000) : 1.f / l_run);
       const uint32_t stage = sbase + C::kOffQ + i * C::kQTileBytes;  // Q_i is no longer read
+      // Partial instances: out = w_new * (this chunk's output) + w_old * (the
+      // output in memory), the weights from the two log-sum-exps.  A side with
+      // no visible key (lse -inf) has weight 0 and is not read into the sum;
+      // when neither side saw a key the row keeps what it holds (NaN).
+      float w_new = 1.f, w_old = 0.f;
+      const uint8_t* orow = nullptr;
+      if constexpr (kPartial) {
+        if (row < S) {
+          float* lp = args.lse + static_cast<int64_t>(b) * args.lse_sb +
+                      static_cast<int64_t>(h) * args.lse_sh + static_cast<int64_t>(row) * args.lse_ss;
+          float lse_out = lse_row;
+          if (args.accumulate) {
+            const float lo = *lp;
+            const float mx2 = fmaxf(lo, lse_row);
+            if (mx2 == -INFINITY) {
+              w_new = 0.f;
+              w_old = 1.f;
+            } else {
+              w_old = lo == -INFINITY ? 0.f : expf(lo - mx2);
+              w_new = lse_row == -INFINITY ? 0.f : expf(lse_row - mx2);
+              const float tot = w_old + w_new;
+              lse_out = mx2 + logf(tot);
+              w_old /= tot;
+              w_new /= tot;
+            }
+            orow = reinterpret_cast<const uint8_t*>(args.o) +
+                   C::ELEM * (static_cast<int64_t>(b) * args.o_sb + static_cast<int64_t>(h) * args.o_sh +
+                              static_cast<int64_t>(row) * args.o_ss);
+          }
+          *lp = lse_out;
+        }
+      }
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
@@ -971,16 +1034,50 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int u = 0; u < 32 / kPer16; ++u) {
           uint32_t w[4];
+          if constexpr (kPartial) {
+            // merge with the 16 bytes of this piece already in the output
+            // (read before the tile's store is issued)
+            uint4 old4 = make_uint4(0u, 0u, 0u, 0u);
+            const int col = 32 * c + kPer16 * u;
+            if (orow && col < args.head_dim)
+              old4 = *reinterpret_cast<const uint4*>(orow + C::ELEM * col);
+            const uint32_t ow[4] = {old4.x, old4.y, old4.z, old4.w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            if constexpr (kTF32) {
-              const float a = __uint_as_float(o[4 * u + e]) * inv_l;
-              w[e] = __float_as_uint(zero_row ? 0.f : a);
-            } else {
-              float a = __uint_as_float(o[8 * u + 2 * e]) * inv_l;
-              float bb = __uint_as_float(o[8 * u + 2 * e + 1]) * inv_l;
-              if (zero_row) a = bb = 0.f;
-              w[e] = pack2<kBF16>(a, bb);
+            for (int e = 0; e < 4; ++e) {
+              if constexpr (kTF32) {
+                const float a = __uint_as_float(o[4 * u + e]) * inv_l;
+                float r = w_new > 0.f ? w_new * a : 0.f;
+                if (w_old > 0.f) r += w_old * __uint_as_float(ow[e]);
+                if (w_new == 0.f && w_old == 1.f) r = __uint_as_float(ow[e]);
+                w[e] = __float_as_uint(r);
+              } else {
+                const float a = __uint_as_float(o[8 * u + 2 * e]) * inv_l;
+                const float bb = __uint_as_float(o[8 * u + 2 * e + 1]) * inv_l;
+                const float oa = kBF16 ? __uint_as_float(ow[e] << 16)
+                                       : __half2float(__ushort_as_half(static_cast<uint16_t>(ow[e])));
+                const float ob = kBF16 ? __uint_as_float(ow[e] & 0xffff0000u)
+                                       : __half2float(__ushort_as_half(static_cast<uint16_t>(ow[e] >> 16)));
+                float ra = w_new > 0.f ? w_new * a : 0.f;
+                float rb = w_new > 0.f ? w_new * bb : 0.f;
+                if (w_old > 0.f) {
+                  ra += w_old * oa;
+                  rb += w_old * ob;
+                }
+                w[e] = (w_new == 0.f && w_old == 1.f) ? ow[e] : pack2<kBF16>(ra, rb);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if constexpr (kTF32) {
+                const float a = __uint_as_float(o[4 * u + e]) * inv_l;
+                w[e] = __float_as_uint(zero_row ? 0.f : a);
+              } else {
+                float a = __uint_as_float(o[8 * u + 2 * e]) * inv_l;
+                float bb = __uint_as_float(o[8 * u + 2 * e + 1]) * inv_l;
+                if (zero_row) a = bb = 0.f;
+                w[e] = pack2<kBF16>(a, bb);
+              }
             }
           }
           const int col = 32 * c + kPer16 * u;  // first element of this 16-byte piece
@@ -1134,9 +1231,10 @@ struct DeviceState {
 };
 DeviceState g_dev[kMaxDevices];
 
-template <class Cf, bool Ca, bool M, int DT, bool SP = false>
-int launch_one(const CUtensorMap maps[4], const KernelArgs& args, int device, cudaStream_t stream) {
-  auto kernel = attn_fwd_sm100_kernel<Cf, Ca, M, DT, SP>;
+template <class Cf, bool Ca, bool M, int DT, bool SP = false, bool PT = false>
+int launch_one(const CUtensorMap maps[4], const typename ArgsOf<PT>::type& args, int device,
+               cudaStream_t stream) {
+  auto kernel = attn_fwd_sm100_kernel<Cf, Ca, M, DT, SP, PT>;
   static std::once_flag attr_once[kMaxDevices];
   static cudaError_t attr_err[kMaxDevices];
   std::call_once(attr_once[device], [&] {
@@ -1168,6 +1266,13 @@ int dispatch_flags(const CUtensorMap maps[4], const KernelArgs& a, const b200_at
   }
   return m ? launch_one<Cf, false, true, DT>(maps, a, dev, s)
            : launch_one<Cf, false, false, DT>(maps, a, dev, s);
+}
+
+template <class Cf, int DT>
+int dispatch_partial(const CUtensorMap maps[4], const PartialKernelArgs& a, bool causal, int dev,
+                     cudaStream_t s) {
+  return causal ? launch_one<Cf, true, false, DT, false, true>(maps, a, dev, s)
+                : launch_one<Cf, false, false, DT, false, true>(maps, a, dev, s);
 }
 
 // Kernel instance for (dtype, head_dim): its keys per K/V tile and ring slots.
@@ -1365,6 +1470,40 @@ extern "C" int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream) {
     default:
       return wide_head(p->head_dim) ? dispatch_flags<Cfg128, B200_ATTN_DTYPE_BF16>(maps, a, p, dev, s)
                                     : dispatch_flags<Cfg64, B200_ATTN_DTYPE_BF16>(maps, a, p, dev, s);
+  }
+}
+
+extern "C" int32_t b200_attn_fwd_partial(const b200_attn_partial_params* pp, void* stream) {
+  if (!pp) return B200_ATTN_ERR_INVALID_ARGUMENT;
+  const b200_attn_fwd_params* p = &pp->base;
+  if (p->key_mask || p->zero_masked_queries) return B200_ATTN_ERR_UNSUPPORTED;
+  if (!pp->lse || (reinterpret_cast<uintptr_t>(pp->lse) & 3u) || pp->reserved != 0 ||
+      (pp->accumulate != 0 && pp->accumulate != 1))
+    return B200_ATTN_ERR_INVALID_ARGUMENT;
+  for (int d = 0; d < 3; ++d)
+    if (pp->lse_stride[d] < 0) return B200_ATTN_ERR_INVALID_ARGUMENT;
+  CUtensorMap maps[4];
+  PartialKernelArgs a;
+  int dev = 0;
+  DeviceGuard guard;
+  const int32_t rc = prepare(p, maps, a, dev, guard);
+  if (rc != B200_ATTN_OK) return rc;
+  a.lse = pp->lse;
+  a.lse_sb = pp->lse_stride[0];
+  a.lse_sh = pp->lse_stride[1];
+  a.lse_ss = pp->lse_stride[2];
+  a.accumulate = pp->accumulate;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool c = p->causal != 0;
+  switch (p->dtype) {
+    case B200_ATTN_DTYPE_FP32:
+      return dispatch_partial<CfgF32, B200_ATTN_DTYPE_FP32>(maps, a, c, dev, s);
+    case B200_ATTN_DTYPE_FP16:
+      return wide_head(p->head_dim) ? dispatch_partial<Cfg128, B200_ATTN_DTYPE_FP16>(maps, a, c, dev, s)
+                                    : dispatch_partial<Cfg64, B200_ATTN_DTYPE_FP16>(maps, a, c, dev, s);
+    default:
+      return wide_head(p->head_dim) ? dispatch_partial<Cfg128, B200_ATTN_DTYPE_BF16>(maps, a, c, dev, s)
+                                    : dispatch_partial<Cfg64, B200_ATTN_DTYPE_BF16>(maps, a, c, dev, s);
   }
 }
 
