@@ -6,8 +6,8 @@
 //   p = exp(x - max) / sum(exp(x - max)) in fp32 (IEEE division), rounded once.
 //
 // HBM-bound: one read of the scores and one write of the probabilities.  A row
-// is owned by a group of G threads (a warp for rows up to 1024 keys, up to a
-// 1024-thread CTA for 32768 keys) that holds it in registers, EPT elements per
+// is owned by a group of G threads (a warp for rows up to 2048 keys, up to a
+// 512-thread CTA for 32768 keys) that holds it in registers, EPT elements per
 // thread, loaded with 16-byte vectors when rows are 16-byte aligned; the max
 // and the sum are reduced with warp shuffles (and shared memory across the
 // warps of a group), so every element is read once, exponentiated once and
@@ -123,7 +123,7 @@ __device__ __forceinline__ float2 scaled_pair(float2 x, float scale) {
   return make_float2(E::widen(E::narrow(s.x)), E::widen(E::narrow(s.y)));
 }
 
-// G threads per row (32, 128, 512 or 1024), EPT elements per thread.  VEC:
+// G threads per row (32 to 512), EPT elements per thread.  VEC:
 // rows start on 16-byte boundaries, each thread loads EPT / V vectors of V
 // elements at vector index n * G + t.  Without VEC it loads single elements at
 // n * G + t.  Both are coalesced across the group.
@@ -296,6 +296,139 @@ __global__ void __launch_bounds__(G < 256 ? 256 : G) softmax_rows_kernel(const S
   }
 }
 
+// Warp per row, persistent: each warp walks rows warp, warp + stride, ...
+// and loads the next row's vectors before it reduces and stores the current
+// one, so a warp keeps two rows of loads in flight.  Rows start on 16-byte
+// boundaries (the vector path); EPT elements per lane.  Two CTAs per SM (the
+// register cap of __launch_bounds__): 16 warps, each with its row in
+// registers and the next row's loads in flight.
+template <int EPT, int DT>
+__global__ void __launch_bounds__(256, 2) softmax_warp_rows_kernel(const SmArgs a) {
+  using E = Elem<DT>;
+  using Raw = typename E::Raw;
+  constexpr bool kExact = DT == B200_ATTN_DTYPE_FP32;
+  constexpr float kLog2e = 1.4426950408889634f;
+  constexpr int V = 16 / static_cast<int>(sizeof(Raw));
+  constexpr int NV = EPT / V;
+  static_assert(EPT % V == 0 && EPT % 2 == 0, "whole vectors and pairs per lane");
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  const int64_t S = a.seq;
+  int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+
+  auto load_row = [&](int64_t r, uint4 (&raw)[NV]) {
+    const Raw* xr = static_cast<const Raw*>(a.x) + r * S;
+#pragma unroll
+    for (int n = 0; n < NV; ++n) {
+      const int64_t c0 = static_cast<int64_t>(n * 32 + lane) * V;
+      raw[n] = c0 < S ? *reinterpret_cast<const uint4*>(xr + c0) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+
+  uint4 cur[NV];
+  if (row < a.rows) load_row(row, cur);
+  for (; row < a.rows; row += stride) {
+    // widen this row first, then put the next row's loads in flight: live
+    // are the fp32 row and the next row's raw vectors, not three buffers
+    float x[EPT];
+#pragma unroll
+    for (int n = 0; n < NV; ++n) {
+      const Raw* raw = reinterpret_cast<const Raw*>(&cur[n]);
+#pragma unroll
+      for (int v = 0; v < V; ++v) x[n * V + v] = E::widen(raw[v]);
+    }
+    const int64_t next = row + stride;
+    if (next < a.rows) load_row(next, cur);
+
+    const int64_t q = row % S;
+    const int64_t b = row / (static_cast<int64_t>(a.heads) * S);
+    const uint8_t* mrow = a.mask ? a.mask + b * a.mask_sb : nullptr;
+    const bool mask_vec = mrow && a.mask_ss == 1 && (reinterpret_cast<uintptr_t>(mrow) & (V - 1)) == 0;
+    float m = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < NV; ++n) {
+      const int64_t c0 = static_cast<int64_t>(n * 32 + lane) * V;
+      float* xv = x + n * V;
+#pragma unroll
+      for (int v = 0; v < V; v += 2) {
+        const float2 sp = scaled_pair<DT>(make_float2(xv[v], xv[v + 1]), a.scale);
+        xv[v] = sp.x;
+        xv[v + 1] = sp.y;
+      }
+      if (c0 >= S) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) xv[v] = -INFINITY;
+      } else {
+        if (a.causal && c0 + V - 1 > q) {
+#pragma unroll
+          for (int v = 0; v < V; ++v)
+            if (c0 + v > q) xv[v] = -INFINITY;
+        }
+        if (mrow) {
+          uint8_t mb[V];
+          if (mask_vec) {
+            if constexpr (V == 8) *reinterpret_cast<uint2*>(mb) = *reinterpret_cast<const uint2*>(mrow + c0);
+            else *reinterpret_cast<uint32_t*>(mb) = *reinterpret_cast<const uint32_t*>(mrow + c0);
+          } else {
+#pragma unroll
+            for (int v = 0; v < V; ++v) mb[v] = mrow[(c0 + v) * a.mask_ss];
+          }
+#pragma unroll
+          for (int v = 0; v < V; ++v)
+            if (!mb[v]) xv[v] = -INFINITY;
+        }
+      }
+#pragma unroll
+      for (int v = 0; v < V; ++v) m = fmaxf(m, xv[v]);
+    }
+    m = warp_max(m);
+
+    float sum = 0.f;
+    if constexpr (kExact) {
+#pragma unroll
+      for (int i = 0; i < EPT; ++i) {
+        x[i] = expf(x[i] - m);
+        sum += x[i];
+      }
+    } else {
+      const float2 l2 = make_float2(kLog2e, kLog2e);
+      const float2 nm = make_float2(-m * kLog2e, -m * kLog2e);
+      float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < EPT; i += 2) {
+        const float2 arg = fma2(make_float2(x[i], x[i + 1]), l2, nm);
+        x[i] = ex2_approx(arg.x);
+        x[i + 1] = ex2_approx(arg.y);
+        s2.x += x[i];
+        s2.y += x[i + 1];
+      }
+      sum = s2.x + s2.y;
+    }
+    sum = warp_sum(sum);
+
+    const float inv = kExact ? 0.f : __frcp_rn(sum);
+    Raw* yr = static_cast<Raw*>(a.y) + row * S;
+#pragma unroll
+    for (int n = 0; n < NV; ++n) {
+      const int64_t c0 = static_cast<int64_t>(n * 32 + lane) * V;
+      if (c0 >= S) continue;
+      Raw out[V];
+#pragma unroll
+      for (int v = 0; v < V; v += 2) {
+        if constexpr (kExact) {
+          out[v] = E::narrow(__fdiv_rn(x[n * V + v], sum));
+          out[v + 1] = E::narrow(__fdiv_rn(x[n * V + v + 1], sum));
+        } else {
+          const float2 pv = mul2(make_float2(x[n * V + v], x[n * V + v + 1]), make_float2(inv, inv));
+          out[v] = E::narrow(pv.x);
+          out[v + 1] = E::narrow(pv.y);
+        }
+      }
+      *reinterpret_cast<uint4*>(yr + c0) = *reinterpret_cast<const uint4*>(out);
+    }
+  }
+}
+
 // Rows longer than the register form holds: one 1024-thread CTA per row,
 // three passes (max, sum, write) whose second and third reads of the row come
 // from L2 (a row is at most 256 KB and one CTA per SM is resident).
@@ -340,6 +473,16 @@ __global__ void __launch_bounds__(kLongThreads) softmax_long_kernel(const SmArgs
 
 int64_t elem_bytes(int32_t dtype) { return dtype == B200_ATTN_DTYPE_FP32 ? 4 : 2; }
 
+// The persistent warp-per-row kernel: enough CTAs to fill every SM several
+// times over, each warp walking the rows with a grid stride.
+template <int EPT, int DT>
+void launch_warp_rows(const SmArgs& a, int num_sms, cudaStream_t s) {
+  const int64_t need = (a.rows + 7) / 8;
+  const int64_t cap = static_cast<int64_t>(num_sms) * 8;
+  const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
+  softmax_warp_rows_kernel<EPT, DT><<<grid, 256, 0, s>>>(a);
+}
+
 template <int G, int EPT, int DT>
 void launch_rows(const SmArgs& a, bool vec, cudaStream_t s) {
   constexpr int kRows = (G < 256 ? 256 : G) / G;
@@ -349,15 +492,28 @@ void launch_rows(const SmArgs& a, bool vec, cudaStream_t s) {
   else softmax_rows_kernel<G, EPT, DT, false><<<grid, kThreads, 0, s>>>(a);
 }
 
-// Row groups by row length: 8 or 32 elements per thread, G threads per row.
+// Row groups by row length: the smallest group that covers the row with up
+// to 64 elements per thread.  A warp per row up to 2048 keys needs no
+// barrier, and more rows per SM keep more of the row loads in flight.
 template <int DT>
-void launch(const SmArgs& a, bool vec, cudaStream_t s) {
+void launch(const SmArgs& a, bool vec, int num_sms, cudaStream_t s) {
   const int S = a.seq;
+  // 64 fp32 values per lane fit the two-CTA register budget for 16-bit rows
+  // (raw next-row vectors of 32 registers); fp32 rows take at most 32
+  constexpr int kWarpMax = (DT == B200_ATTN_DTYPE_FP32 ? 32 : 64) * 32;
+  if (vec && S <= kWarpMax) {
+    if (S <= 8 * 32) launch_warp_rows<8, DT>(a, num_sms, s);
+    else if (S <= 32 * 32 || DT == B200_ATTN_DTYPE_FP32) launch_warp_rows<32, DT>(a, num_sms, s);
+    else launch_warp_rows<64, DT>(a, num_sms, s);
+    return;
+  }
   if (S <= 256) launch_rows<32, 8, DT>(a, vec, s);
   else if (S <= 1024) launch_rows<32, 32, DT>(a, vec, s);
-  else if (S <= 4096) launch_rows<128, 32, DT>(a, vec, s);
-  else if (S <= 16384) launch_rows<512, 32, DT>(a, vec, s);
-  else if (S <= kMaxRegisterRow) launch_rows<1024, 32, DT>(a, vec, s);
+  else if (S <= 2048) launch_rows<32, 64, DT>(a, vec, s);
+  else if (S <= 4096) launch_rows<64, 64, DT>(a, vec, s);
+  else if (S <= 8192) launch_rows<128, 64, DT>(a, vec, s);
+  else if (S <= 16384) launch_rows<256, 64, DT>(a, vec, s);
+  else if (S <= kMaxRegisterRow) launch_rows<512, 64, DT>(a, vec, s);
   else softmax_long_kernel<DT><<<static_cast<unsigned>(a.rows), kLongThreads, 0, s>>>(a);
 }
 
@@ -434,10 +590,18 @@ extern "C" int32_t b200_softmax_fwd(const b200_softmax_params* p, void* stream) 
                    ((reinterpret_cast<uintptr_t>(p->scores) |
                      reinterpret_cast<uintptr_t>(p->probs)) & 15u) == 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  static int sms[64] = {0};
+  if (attr.device < 64 && sms[attr.device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, attr.device) != cudaSuccess || n < 1)
+      n = 148;
+    sms[attr.device] = n;
+  }
+  const int num_sms = attr.device < 64 ? sms[attr.device] : 148;
   switch (p->dtype) {
-    case B200_ATTN_DTYPE_BF16: launch<B200_ATTN_DTYPE_BF16>(a, vec, s); break;
-    case B200_ATTN_DTYPE_FP16: launch<B200_ATTN_DTYPE_FP16>(a, vec, s); break;
-    default: launch<B200_ATTN_DTYPE_FP32>(a, vec, s); break;
+    case B200_ATTN_DTYPE_BF16: launch<B200_ATTN_DTYPE_BF16>(a, vec, num_sms, s); break;
+    case B200_ATTN_DTYPE_FP16: launch<B200_ATTN_DTYPE_FP16>(a, vec, num_sms, s); break;
+    default: launch<B200_ATTN_DTYPE_FP32>(a, vec, num_sms, s); break;
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
