@@ -74,6 +74,17 @@ def chunk_pairs(world: int, rank: int, source: int, causal: bool) -> list[tuple[
     return pairs
 
 
+_comm_streams: dict = {}
+
+
+def _comm_stream(device: torch.device) -> "torch.cuda.Stream":
+    """The side stream the ring's K/V exchange runs on (one per device)."""
+    stream = _comm_streams.get(device)
+    if stream is None:
+        stream = _comm_streams[device] = torch.cuda.Stream(device)
+    return stream
+
+
 PartialFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, bool, float, torch.Tensor,
                       torch.Tensor, bool], None]
 
@@ -98,7 +109,7 @@ def ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
     started = [False, False]
     kv = torch.stack([k, v]).contiguous()  # [2, B, H, 2L, D]: this rank's K/V share
     recv = torch.empty_like(kv) if world > 1 else None
-    comm = torch.cuda.Stream(q.device) if (world > 1 and q.is_cuda) else None
+    comm = _comm_stream(q.device) if (world > 1 and q.is_cuda) else None
     compute = torch.cuda.current_stream(q.device) if q.is_cuda else None
     for step in range(world):
         source = (rank - step) % world

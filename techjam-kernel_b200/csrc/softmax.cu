@@ -19,6 +19,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <mutex>
 
 #include "b200_softmax.h"
 #include "byte_range.h"
@@ -524,6 +525,23 @@ struct DeviceGuard {
   }
 };
 
+// SMs of a device, queried once per device (the persistent kernel's grid).
+int sm_count(int device) {
+  constexpr int kMaxDevices = 64;
+  static std::once_flag once[kMaxDevices];
+  static int sms[kMaxDevices];
+  if (device < 0 || device >= kMaxDevices) return 148;
+  std::call_once(once[device], [device] {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      n = 148;
+    }
+    sms[device] = n;
+  });
+  return sms[device];
+}
+
 }  // namespace b200sm
 
 using namespace b200sm;
@@ -590,14 +608,7 @@ extern "C" int32_t b200_softmax_fwd(const b200_softmax_params* p, void* stream) 
                    ((reinterpret_cast<uintptr_t>(p->scores) |
                      reinterpret_cast<uintptr_t>(p->probs)) & 15u) == 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  static int sms[64] = {0};
-  if (attr.device < 64 && sms[attr.device] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, attr.device) != cudaSuccess || n < 1)
-      n = 148;
-    sms[attr.device] = n;
-  }
-  const int num_sms = attr.device < 64 ? sms[attr.device] : 148;
+  const int num_sms = sm_count(attr.device);
   switch (p->dtype) {
     case B200_ATTN_DTYPE_BF16: launch<B200_ATTN_DTYPE_BF16>(a, vec, num_sms, s); break;
     case B200_ATTN_DTYPE_FP16: launch<B200_ATTN_DTYPE_FP16>(a, vec, num_sms, s); break;

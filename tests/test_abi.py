@@ -197,3 +197,43 @@ def test_packed_layout_fills_every_field_in_order():
     assert list(p.q_stride) + list(p.k_stride) + list(p.v_stride) + list(p.o_stride) == ints[8:20]
     assert p.key_mask == 21 and list(p.mask_stride) == [22, 23]
     assert (p.scale, p.dtype, p.causal, p.zero_masked_queries, p.error_word) == (0.25, 26, 27, 28, 29)
+
+
+def test_partial_entry_point_rejects_what_it_does_not_take(lib):
+    """b200_attn_fwd_partial refuses key masks, zeroed queries and a missing or
+    misaligned log-sum-exp buffer before touching the device."""
+    def call(**kw):
+        pp = _native.PartialParams()
+        pp.base = _params()
+        pp.lse = 0x20000
+        pp.lse_stride[:] = (4 * 256, 256, 1)
+        for key, val in kw.items():
+            if key.startswith("base_"):
+                setattr(pp.base, key[5:], val)
+            else:
+                setattr(pp, key, val)
+        return lib.b200_attn_fwd_partial(ctypes.byref(pp), None)
+
+    assert call(base_key_mask=0x30000) == _native.ERR_UNSUPPORTED
+    assert call(base_zero_masked_queries=1) == _native.ERR_UNSUPPORTED
+    assert call(lse=0) == _native.ERR_INVALID_ARGUMENT
+    assert call(lse=0x20002) == _native.ERR_INVALID_ARGUMENT
+    assert call(accumulate=2) == _native.ERR_INVALID_ARGUMENT
+    assert call(reserved=1) == _native.ERR_INVALID_ARGUMENT
+    assert lib.b200_attn_fwd_partial(None, None) == _native.ERR_INVALID_ARGUMENT
+
+
+def test_partial_params_layout_matches_c(tmp_path):
+    fields = [f for f, _ in _native.PartialParams._fields_]
+    src = tmp_path / "layout.c"
+    body = "\n".join(f'  printf("{f} %zu\\n", offsetof(b200_attn_partial_params, {f}));' for f in fields)
+    src.write_text(f'#include <stdio.h>\n#include <stddef.h>\n#include "b200_attn.h"\n'
+                   f'int main(void) {{\n  printf("size %zu\\n", sizeof(b200_attn_partial_params));\n{body}\n'
+                   f'  return 0;\n}}\n')
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", f"-I{ROOT / 'include'}", str(src), "-o", str(exe)], check=True)
+    lines = dict(l.split() for l in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                   check=True).stdout.splitlines())
+    assert int(lines["size"]) == ctypes.sizeof(_native.PartialParams)
+    for f in fields:
+        assert int(lines[f]) == getattr(_native.PartialParams, f).offset, f
