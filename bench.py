@@ -302,10 +302,55 @@ class CpuReference:
         return out
 
 
+def run_reference_softmax_arm(args, cfg: dict, world: int) -> int:
+    """Reference arm of the softmax workload: the reference's softmax stage
+    (oracle.reference_softmax, torch CPU ops in its order) on host cores, on one
+    batch entry of the score tensor, in the GPU arm's unit (GB/s)."""
+    import torch
+
+    from oracle.reference_attention import reference_softmax
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, H, _ = shard_for(cfg, 1, 0)
+    S, D = cfg["S"], cfg["D"]
+    dtype = cfg_dtype(cfg)
+    elem = torch.finfo(dtype).bits // 8
+    heads = max(1, min(H, int(2 ** 31 // (S * S * 12))))
+    gen = torch.Generator("cpu").manual_seed(args.seed)
+    scores = (4 * torch.randn((1, heads, S, S), generator=gen)).to(dtype)
+    for _ in range(args.warmup):
+        reference_softmax(scores, None, D ** -0.5, cfg["causal"])
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        reference_softmax(scores, None, D ** -0.5, cfg["causal"])
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    sample_bytes = 2.0 * heads * S * S * elem
+    value = sample_bytes / sec / 1e9
+    desc = (f"oracle.reference_softmax (torch CPU, reference op order) on [1,{heads},{S},{S}] "
+            f"{dtype_tag(cfg)}; {args.steps} timed reps")
+    print(json.dumps({
+        "impl": "reference", "metric": "row softmax over materialised attention scores, GB/s",
+        "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 2.0 * B * H * S * S * elem / (value * 1e9) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": dtype_tag(cfg),
+        "data": "synthetic (seeded 4 * N(0,1) scores)",
+        "config": {"workload": args.workload, "B": B, "H": H, "S": S, "causal": cfg["causal"],
+                   "impl_path": "oracle.reference_softmax on host CPU cores"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
 def run_reference_arm(args, cfg: dict, rank: int, world: int) -> int:
     """Reference arm: the reference's CPU attention on host cores, rank 0 only."""
     if rank != 0:
         return 0
+    if cfg.get("kind") == "softmax":
+        return run_reference_softmax_arm(args, cfg, world)
     ref = CpuReference(cfg, args.seed)
     for _ in range(args.warmup):
         ref.call()

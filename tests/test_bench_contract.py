@@ -80,3 +80,14 @@ def test_default_workload_is_the_largest_single_gpu_config():
     assert 'ap.add_argument("--workload", default="cfg4"' in src
     assert bench.WORKLOADS["cfg4"]["shard"] == "heads"
     del args
+
+
+def test_reference_arm_of_the_softmax_workload_times_the_softmax():
+    proc = subprocess.run(
+        [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", "sm2",
+         "--steps", "1", "--warmup", "3", "--heads", "1"],
+        capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    d = json.loads([l for l in proc.stdout.splitlines() if l.startswith("{")][-1])
+    assert d["impl"] == "reference" and d["unit"] == "GB/s" and d["value"] > 0
+    assert "reference_softmax" in d["cpu_baseline"]["sample"]

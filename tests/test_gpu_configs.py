@@ -121,3 +121,27 @@ def test_autograd_routes_to_the_exact_path_on_cuda():
     assert plan.mode == AttentionMode.EXACT_REFERENCE
     out.float().sum().backward()
     assert x.grad is not None and torch.isfinite(x.grad.float()).all()
+
+
+def test_bench_line_carries_the_contract_fields():
+    """bench.py on one GPU (short cfg1 run): the JSON line has the fields the
+    benchmark contract asks for, counted launches and a clock record."""
+    import subprocess
+    import sys
+
+    root = Path(__file__).resolve().parents[1]
+    proc = subprocess.run([sys.executable, str(root / "bench.py"), "--workload", "cfg1", "--steps", "16",
+                           "--warmup", "3", "--cpu-budget", "0.5", "--e2e-steps", "3"],
+                          capture_output=True, text=True, timeout=600, cwd=root)
+    assert proc.returncode == 0, proc.stderr[-3000:]
+    d = json.loads([l for l in proc.stdout.splitlines() if l.startswith("{")][-1])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "roofline", "cpu_baseline", "e2e", "gpu_launches", "clocks"):
+        assert key in d, key
+    r = d["roofline"]
+    assert r["bound"] == "hbm" and r["unit"] == "GB/s" and 0 < r["frac"] < 1.5
+    assert r["tensor"]["unit"] == "TFLOP/s" and r["traffic_source"]["file"].startswith("profiles/")
+    assert d["gpu_launches"] == 16 and d["validation"]["device_errors"] == 0
+    assert d["e2e"]["h2d_bytes_per_step"] > 0 and d["e2e"]["d2h_bytes_per_step"] > 0
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
