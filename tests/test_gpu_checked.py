@@ -80,3 +80,31 @@ def test_checked_build_odd_shapes(dtype, B, H, S, D, causal, lengths, zero_q):
     if zero_q:
         ref = zero_masked_rows(ref, mask)
     assert_close(out, ref, f"checked {dtype} B{B} H{H} S{S} D{D}")
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float16, 64), (torch.float32, 64)])
+def test_checked_build_partial_form(dtype, D):
+    """The context-parallel partial instances in the bounds-checked build: a
+    diagonal chunk, then an earlier chunk merged in (accumulate); the word
+    stays clear and the merge equals attention over both chunks."""
+    dev = torch.device("cuda", 0)
+    lib = _native.load_checked_library()
+    L = 300
+    q, k, v = seeded_qkv((1, 2, 2 * L, D), dtype, 91)
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    out = torch.empty((1, 2, L, D), device=dev, dtype=dtype)
+    lse = torch.empty((1, 2, L), device=dev, dtype=torch.float32)
+    read_device_errors(dev)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    for k_lo, causal, acc in ((L, True, 0), (0, False, 1)):  # query chunk = rows L..2L
+        pp = _native.PartialParams()
+        pp.base = make_params(qd[:, :, L:], kd[:, :, k_lo:k_lo + L], vd[:, :, k_lo:k_lo + L], out,
+                              None, causal, D ** -0.5, False, device_error_word(dev))
+        pp.lse = lse.data_ptr()
+        pp.lse_stride[:] = (lse.stride(0), lse.stride(1), lse.stride(2))
+        pp.accumulate = acc
+        assert lib.b200_attn_fwd_partial(ctypes.byref(pp), stream) == _native.OK
+    torch.cuda.synchronize(dev)
+    assert read_device_errors(dev) == 0, "a bounds check failed"
+    ref = reference_attention(q, k, v, None, True, D ** -0.5)[:, :, L:]
+    assert_close(out, ref, f"checked partial {dtype}")
