@@ -496,12 +496,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool early_k0 = !(kStallProbe && args.skip_load == 0);
 
   // ---------------------------------------------------------- prologue
+  // Launched with programmatic stream serialization: the next kernel in the
+  // stream may start its set-up now, and this CTA's set-up (barriers, TMEM,
+  // tensor-map prefetch) overlaps the previous kernel's tail.  No thread
+  // touches global memory before grid_dependency_wait.
+  if (threadIdx.x == 0) ptx::launch_dependents();
   if (warp == kLoadWarp) {
-    int extent = S;
-    if constexpr (kMask) extent = mask_extent(mrow, args.mask_ss, S, lane);
     if (lane == 0) {
       misc[1] = 0u;
-      misc[2] = static_cast<uint32_t>(extent);
       ptx::mbar_init(bar(C::kBarQ), 1);
       ptx::mbar_init(bar(C::kBarQ + 1), 1);
       for (int s = 0; s < NSLOT; ++s) {
@@ -526,6 +528,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tma_prefetch_desc(&tm_k);
       ptx::tma_prefetch_desc(&tm_v);
       ptx::tma_prefetch_desc(&tm_o);
+    }
+    ptx::grid_dependency_wait();
+    int extent = S;
+    if constexpr (kMask) extent = mask_extent(mrow, args.mask_ss, S, lane);
+    if (lane == 0) {
+      misc[2] = static_cast<uint32_t>(extent);
       // Q0, K(0), Q1 overlap the set-up below; the first product needs only
       // Q0 and K(0).  A block that returns at once (all its query rows
       // masked) loads nothing.
@@ -540,6 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   __syncthreads();
+  if (warp != kLoadWarp) ptx::grid_dependency_wait();
   const int extent = static_cast<int>(misc[2]);
 
   // A block whose rows all lie at or past the last valid key has only masked
@@ -1276,8 +1285,18 @@ int launch_one(const CUtensorMap maps[4], const typename ArgsOf<PT>::type& args,
     return B200_ATTN_ERR_LAUNCH;
   }
   const unsigned grid = static_cast<unsigned>(args.num_q_blocks) * args.batch * args.heads;
-  kernel<<<grid, kThreads, Cf::kSmemBytes, stream>>>(maps[0], maps[1], maps[2], maps[3], args);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cf::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], maps[3], args);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(cudaGetErrorString(e));
     return B200_ATTN_ERR_LAUNCH;
