@@ -341,14 +341,22 @@ __global__ void __launch_bounds__(256, 2) softmax_warp_rows_kernel(const SmArgs 
     const int64_t next = row + stride;
     if (next < a.rows) load_row(next, cur);
 
-    const int64_t q = row % S;
+    // 32-bit column arithmetic (S <= B200_SOFTMAX_MAX_SEQ).  A chunk n covers
+    // the warp's columns [n * 32 * V, (n + 1) * 32 * V); with causality every
+    // chunk that starts past this row's query index holds only -inf scores,
+    // whose probabilities are exact zeros: the warp skips their arithmetic
+    // (a warp-uniform test) and stores zeros.
+    const int Si = static_cast<int>(S);
+    const int q = static_cast<int>(row % S);
     const int64_t b = row / (static_cast<int64_t>(a.heads) * S);
     const uint8_t* mrow = a.mask ? a.mask + b * a.mask_sb : nullptr;
     const bool mask_vec = mrow && a.mask_ss == 1 && (reinterpret_cast<uintptr_t>(mrow) & (V - 1)) == 0;
+    auto chunk_live = [&](int n) { return n * 32 * V < Si && !(a.causal && n * 32 * V > q); };
     float m = -INFINITY;
 #pragma unroll
     for (int n = 0; n < NV; ++n) {
-      const int64_t c0 = static_cast<int64_t>(n * 32 + lane) * V;
+      if (!chunk_live(n)) continue;
+      const int c0 = (n * 32 + lane) * V;
       float* xv = x + n * V;
 #pragma unroll
       for (int v = 0; v < V; v += 2) {
@@ -356,7 +364,7 @@ __global__ void __launch_bounds__(256, 2) softmax_warp_rows_kernel(const SmArgs 
         xv[v] = sp.x;
         xv[v + 1] = sp.y;
       }
-      if (c0 >= S) {
+      if (c0 >= Si) {
 #pragma unroll
         for (int v = 0; v < V; ++v) xv[v] = -INFINITY;
       } else {
@@ -372,7 +380,7 @@ __global__ void __launch_bounds__(256, 2) softmax_warp_rows_kernel(const SmArgs 
             else *reinterpret_cast<uint32_t*>(mb) = *reinterpret_cast<const uint32_t*>(mrow + c0);
           } else {
 #pragma unroll
-            for (int v = 0; v < V; ++v) mb[v] = mrow[(c0 + v) * a.mask_ss];
+            for (int v = 0; v < V; ++v) mb[v] = mrow[static_cast<int64_t>(c0 + v) * a.mask_ss];
           }
 #pragma unroll
           for (int v = 0; v < V; ++v)
@@ -387,21 +395,31 @@ __global__ void __launch_bounds__(256, 2) softmax_warp_rows_kernel(const SmArgs 
     float sum = 0.f;
     if constexpr (kExact) {
 #pragma unroll
-      for (int i = 0; i < EPT; ++i) {
-        x[i] = expf(x[i] - m);
-        sum += x[i];
+      for (int n = 0; n < NV; ++n) {
+        if (!chunk_live(n)) continue;
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          const int i = n * V + v;
+          x[i] = expf(x[i] - m);
+          sum += x[i];
+        }
       }
     } else {
       const float2 l2 = make_float2(kLog2e, kLog2e);
       const float2 nm = make_float2(-m * kLog2e, -m * kLog2e);
       float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < EPT; i += 2) {
-        const float2 arg = fma2(make_float2(x[i], x[i + 1]), l2, nm);
-        x[i] = ex2_approx(arg.x);
-        x[i + 1] = ex2_approx(arg.y);
-        s2.x += x[i];
-        s2.y += x[i + 1];
+      for (int n = 0; n < NV; ++n) {
+        if (!chunk_live(n)) continue;
+#pragma unroll
+        for (int v = 0; v < V; v += 2) {
+          const int i = n * V + v;
+          const float2 arg = fma2(make_float2(x[i], x[i + 1]), l2, nm);
+          x[i] = ex2_approx(arg.x);
+          x[i + 1] = ex2_approx(arg.y);
+          s2.x += x[i];
+          s2.y += x[i + 1];
+        }
       }
       sum = s2.x + s2.y;
     }
@@ -411,18 +429,26 @@ __global__ void __launch_bounds__(256, 2) softmax_warp_rows_kernel(const SmArgs 
     Raw* yr = static_cast<Raw*>(a.y) + row * S;
 #pragma unroll
     for (int n = 0; n < NV; ++n) {
-      const int64_t c0 = static_cast<int64_t>(n * 32 + lane) * V;
-      if (c0 >= S) continue;
+      const int c0 = (n * 32 + lane) * V;
+      if (c0 >= Si) continue;
       Raw out[V];
+      if (!chunk_live(n)) {
+        // a row with no visible key is NaN throughout, as torch.softmax of
+        // an all -inf row
+        const float z = m == -INFINITY ? __int_as_float(0x7fc00000) : 0.f;
 #pragma unroll
-      for (int v = 0; v < V; v += 2) {
-        if constexpr (kExact) {
-          out[v] = E::narrow(__fdiv_rn(x[n * V + v], sum));
-          out[v + 1] = E::narrow(__fdiv_rn(x[n * V + v + 1], sum));
-        } else {
-          const float2 pv = mul2(make_float2(x[n * V + v], x[n * V + v + 1]), make_float2(inv, inv));
-          out[v] = E::narrow(pv.x);
-          out[v + 1] = E::narrow(pv.y);
+        for (int v = 0; v < V; ++v) out[v] = E::narrow(z);
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; v += 2) {
+          if constexpr (kExact) {
+            out[v] = E::narrow(__fdiv_rn(x[n * V + v], sum));
+            out[v + 1] = E::narrow(__fdiv_rn(x[n * V + v + 1], sum));
+          } else {
+            const float2 pv = mul2(make_float2(x[n * V + v], x[n * V + v + 1]), make_float2(inv, inv));
+            out[v] = E::narrow(pv.x);
+            out[v + 1] = E::narrow(pv.y);
+          }
         }
       }
       *reinterpret_cast<uint4*>(yr + c0) = *reinterpret_cast<const uint4*>(out);

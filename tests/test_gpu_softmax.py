@@ -77,6 +77,20 @@ def test_softmax_in_place_and_fully_masked_rows():
     assert_within_units(out, ref, 1, "in place")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_softmax_causal_rows_with_no_visible_key_are_nan(dtype):
+    # Causal rows skip the column chunks past their query index; a row whose
+    # visible keys are all masked must still be NaN in those chunks too.
+    B, H, S, D = 2, 2, 1024, 64
+    scores = _scores((B, H, S, D), dtype, 11)
+    mask = prefix_mask(B, S, [S, 0])
+    ref = reference_softmax(scores, mask, D ** -0.5, True)
+    out = b200_attention_softmax(scores.to(DEV), mask.to(DEV), D ** -0.5, True)
+    torch.cuda.synchronize()
+    assert torch.isnan(out[1].float()).all()
+    assert_within_units(out, ref, UNITS[dtype], f"{dtype} causal, no visible key")
+
+
 @pytest.mark.parametrize("S", [16384, 32768])
 def test_softmax_long_rows_in_registers(S):
     scores = _scores((1, 1, S, 32), torch.bfloat16, 11)
