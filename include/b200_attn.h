@@ -132,7 +132,10 @@ B200_ATTN_API int32_t b200_attn_check(const b200_attn_fwd_params* p);
 /* Launch the forward on `stream` (a cudaStream_t of the tensors' device; NULL =
  * legacy default stream).  The device is taken from the q pointer; the caller's
  * current device is left as it was.  Asynchronous: no device synchronisation,
- * no allocation.  Replaces the kernel
+ * no allocation.  The kernel is launched with programmatic stream
+ * serialization: its set-up may overlap the previous kernel's tail, and it
+ * touches global memory only after that kernel has completed, so stream order
+ * holds as for a plain launch.  Replaces the kernel
  * launch of triton_fused_attention (model/triton_fused_attention.py:1968-2001). */
 B200_ATTN_API int32_t b200_attn_fwd(const b200_attn_fwd_params* p, void* stream);
 
