@@ -49,17 +49,33 @@ struct SmArgs {
 // Element type traits: widen to fp32, round an fp32 value to the type.
 template <int DT>
 struct Elem;
+// narrow2 / widen2: a pair in one 32-bit word (low half first), rounded
+// like two narrow calls.
 template <>
 struct Elem<B200_ATTN_DTYPE_BF16> {
   using Raw = uint16_t;
   __device__ static float widen(Raw v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
   __device__ static Raw narrow(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+  __device__ static uint32_t narrow2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
+  __device__ static float2 widen2(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  }
 };
 template <>
 struct Elem<B200_ATTN_DTYPE_FP16> {
   using Raw = uint16_t;
   __device__ static float widen(Raw v) { return __half2float(__ushort_as_half(v)); }
   __device__ static Raw narrow(float x) { return __half_as_ushort(__float2half_rn(x)); }
+  __device__ static uint32_t narrow2(float lo, float hi) {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
+  __device__ static float2 widen2(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  }
 };
 template <>
 struct Elem<B200_ATTN_DTYPE_FP32> {
@@ -121,7 +137,22 @@ template <int DT>
 __device__ __forceinline__ float2 scaled_pair(float2 x, float scale) {
   using E = Elem<DT>;
   const float2 s = mul2(x, make_float2(scale, scale));
-  return make_float2(E::widen(E::narrow(s.x)), E::widen(E::narrow(s.y)));
+  if constexpr (DT == B200_ATTN_DTYPE_FP32) return s;
+  else return E::widen2(E::narrow2(s.x, s.y));
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+// Three-input maximum (sm_100 max.f32 with three sources).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // G threads per row (32 to 512), EPT elements per thread.  VEC:
@@ -388,7 +419,7 @@ __global__ void __launch_bounds__(256, 2) softmax_warp_rows_kernel(const SmArgs 
         }
       }
 #pragma unroll
-      for (int v = 0; v < V; ++v) m = fmaxf(m, xv[v]);
+      for (int v = 0; v < V; v += 2) m = fmax3(m, xv[v], xv[v + 1]);
     }
     m = warp_max(m);
 
@@ -417,8 +448,7 @@ __global__ void __launch_bounds__(256, 2) softmax_warp_rows_kernel(const SmArgs 
           const float2 arg = fma2(make_float2(x[i], x[i + 1]), l2, nm);
           x[i] = ex2_approx(arg.x);
           x[i + 1] = ex2_approx(arg.y);
-          s2.x += x[i];
-          s2.y += x[i + 1];
+          s2 = add2(s2, make_float2(x[i], x[i + 1]));
         }
       }
       sum = s2.x + s2.y;
@@ -446,8 +476,7 @@ __global__ void __launch_bounds__(256, 2) softmax_warp_rows_kernel(const SmArgs 
             out[v + 1] = E::narrow(__fdiv_rn(x[n * V + v + 1], sum));
           } else {
             const float2 pv = mul2(make_float2(x[n * V + v], x[n * V + v + 1]), make_float2(inv, inv));
-            out[v] = E::narrow(pv.x);
-            out[v + 1] = E::narrow(pv.y);
+            *reinterpret_cast<uint32_t*>(&out[v]) = E::narrow2(pv.x, pv.y);
           }
         }
       }
