@@ -193,6 +193,37 @@ typedef struct b200_attn_partial_params {
 
 B200_ATTN_API int32_t b200_attn_fwd_partial(const b200_attn_partial_params* p, void* stream);
 
+/* Largest batch * heads * seq_len b200_attn_fwd_partial_static takes: its
+ * log-sum-exp array holds this many fp32 values (4 MiB) on every device. */
+#define B200_ATTN_STATIC_LSE_MAX_ROWS (1 << 20)
+
+/* Allocation-free form of b200_attn_fwd_partial (no counterpart in the
+ * reference, which allocates every buffer through torch).  It is for callers
+ * that cannot call cudaMalloc: a host whose memory pool already owns the
+ * device's memory, a loop that cannot take the device-wide synchronisation of
+ * cudaMalloc/cudaFree, or a foreign-language binding with no device allocator.
+ * Such a caller passes q, k, v and o as for b200_attn_fwd_partial (base.key_mask
+ * NULL, base.zero_masked_queries 0); the per-row log-sum-exp that carries one
+ * query chunk's merge from call to call lives in a fixed array inside this
+ * library instead of a caller buffer, so nothing is allocated.
+ *   - Limit: batch * heads * seq_len <= B200_ATTN_STATIC_LSE_MAX_ROWS, else
+ *     B200_ATTN_ERR_INVALID_ARGUMENT and nothing is launched.
+ *   - accumulate = 0 writes every row's log-sum-exp (nothing needs clearing);
+ *     accumulate = 1 merges into what the last call on this device left, and
+ *     is refused (B200_ATTN_ERR_INVALID_ARGUMENT) unless the last launched
+ *     first-chunk call on this device had the same batch, heads and seq_len.
+ *   - The array is shared by every call on a device and keeps the last call's
+ *     contents: calls that overlap on the GPU (two streams, or another query
+ *     chunk's first call between a chunk's calls) race and give undefined
+ *     output.  Issue one query chunk's calls in order on one stream.
+ *   - The first call on each device looks up the array's device address
+ *     (once, with that device current); make that first call before any
+ *     stream capture.  The array itself occupies its 4 MiB on every device
+ *     that loads the library, until the process exits.
+ * Return codes and the error word are those of b200_attn_fwd_partial. */
+B200_ATTN_API int32_t b200_attn_fwd_partial_static(const b200_attn_fwd_params* p,
+                                                   int32_t accumulate, void* stream);
+
 /* Self-test of failure detection (no reference counterpart).  Launches the
  * forward exactly like b200_attn_fwd, except that in every CTA the K/V load
  * number `skipped_load` (0 = first K tile, 1 = first V tile, ...) is announced

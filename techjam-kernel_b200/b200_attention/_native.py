@@ -46,6 +46,7 @@ EXPORTED_SYMBOLS = (
     "b200_attn_launch_count",
     "b200_attn_launch_shape",
     "b200_attn_fwd_partial",
+    "b200_attn_fwd_partial_static",
 )
 # Every symbol ``include/b200_linear.h`` declares.
 LINEAR_SYMBOLS = (
@@ -202,6 +203,9 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         ctypes.POINTER(ctypes.c_int32)] * 5
     lib.b200_attn_fwd_partial.restype = ctypes.c_int32
     lib.b200_attn_fwd_partial.argtypes = [ctypes.POINTER(PartialParams), ctypes.c_void_p]
+    lib.b200_attn_fwd_partial_static.restype = ctypes.c_int32
+    lib.b200_attn_fwd_partial_static.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_int32,
+                                                 ctypes.c_void_p]
     lib.b200_attn_selftest_stall.restype = ctypes.c_int32
     lib.b200_attn_selftest_stall.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_int32,
                                              ctypes.c_void_p]

@@ -1571,3 +1571,97 @@ extern "C" int32_t b200_attn_selftest_stall(const b200_attn_fwd_params* p, int32
   return launch_one<Cfg128, true, false, B200_ATTN_DTYPE_BF16, true>(
       maps, a, dev, reinterpret_cast<cudaStream_t>(stream));
 }
+
+// ------------------------------------------- allocation-free partial step
+// Log-sum-exp scratch of b200_attn_fwd_partial_static: one fp32 per (batch,
+// head, query row), [B, H, S] contiguous.  It is a module variable, so every
+// device that loads this library holds its 4 MiB until the process exits, and
+// every call on a device shares it.  Host code must not pass its name to a
+// kernel (on the host the name is only a stand-in); the entry point looks up
+// its device address once per device instead.
+static __device__ __align__(256) float b200_static_lse[B200_ATTN_STATIC_LSE_MAX_ROWS];
+
+namespace b200attn {
+namespace {
+
+struct StaticLseState {
+  std::once_flag resolved;
+  cudaError_t err = cudaSuccess;
+  float* ptr = nullptr;  // device address of b200_static_lse on this device
+  std::mutex mu;
+  // Shape of the last first-chunk call that launched on this device; an
+  // accumulating call must match it (its rows merge into what that call left).
+  int64_t shape[3] = {0, 0, 0};
+};
+StaticLseState g_static_lse[kMaxDevices];
+
+}  // namespace
+}  // namespace b200attn
+
+extern "C" int32_t b200_attn_fwd_partial_static(const b200_attn_fwd_params* p, int32_t accumulate,
+                                                void* stream) {
+  if (!p) return B200_ATTN_ERR_INVALID_ARGUMENT;
+  if (p->key_mask || p->zero_masked_queries) return B200_ATTN_ERR_UNSUPPORTED;
+  if (accumulate != 0 && accumulate != 1) return B200_ATTN_ERR_INVALID_ARGUMENT;
+  int32_t rc = b200_attn_check(p);
+  if (rc != B200_ATTN_OK) return rc;
+  // batch * heads <= 2^24 and seq_len <= 2^30 (b200_attn_check): no overflow
+  const int64_t rows = p->batch * p->heads * p->seq_len;
+  if (rows > B200_ATTN_STATIC_LSE_MAX_ROWS) {
+    set_error("batch * heads * seq_len exceeds B200_ATTN_STATIC_LSE_MAX_ROWS");
+    return B200_ATTN_ERR_INVALID_ARGUMENT;
+  }
+  CUtensorMap maps[4];
+  PartialKernelArgs a;
+  int dev = 0;
+  DeviceGuard guard;
+  rc = prepare(p, maps, a, dev, guard);  // leaves `dev` current until return
+  if (rc != B200_ATTN_OK) return rc;
+  StaticLseState& st = g_static_lse[dev];
+  std::call_once(st.resolved, [&st] {
+    st.err = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.ptr), b200_static_lse);
+    if (st.err != cudaSuccess) {
+      cudaGetLastError();
+      st.ptr = nullptr;
+    }
+  });
+  if (st.err != cudaSuccess || !st.ptr) {
+    set_error(st.err != cudaSuccess ? cudaGetErrorString(st.err)
+                                    : "no device address for the static log-sum-exp array");
+    return B200_ATTN_ERR_DEVICE;
+  }
+  if (accumulate) {
+    std::lock_guard<std::mutex> lk(st.mu);
+    if (st.shape[0] != p->batch || st.shape[1] != p->heads || st.shape[2] != p->seq_len) {
+      set_error("accumulating call without a first-chunk call of the same shape on this device");
+      return B200_ATTN_ERR_INVALID_ARGUMENT;
+    }
+  }
+  a.lse = st.ptr;
+  a.lse_sb = p->heads * p->seq_len;
+  a.lse_sh = p->seq_len;
+  a.lse_ss = 1;
+  a.accumulate = accumulate;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool c = p->causal != 0;
+  switch (p->dtype) {
+    case B200_ATTN_DTYPE_FP32:
+      rc = dispatch_partial<CfgF32, B200_ATTN_DTYPE_FP32>(maps, a, c, dev, s);
+      break;
+    case B200_ATTN_DTYPE_FP16:
+      rc = wide_head(p->head_dim) ? dispatch_partial<Cfg128, B200_ATTN_DTYPE_FP16>(maps, a, c, dev, s)
+                                  : dispatch_partial<Cfg64, B200_ATTN_DTYPE_FP16>(maps, a, c, dev, s);
+      break;
+    default:
+      rc = wide_head(p->head_dim) ? dispatch_partial<Cfg128, B200_ATTN_DTYPE_BF16>(maps, a, c, dev, s)
+                                  : dispatch_partial<Cfg64, B200_ATTN_DTYPE_BF16>(maps, a, c, dev, s);
+      break;
+  }
+  if (rc == B200_ATTN_OK && !accumulate) {
+    std::lock_guard<std::mutex> lk(st.mu);
+    st.shape[0] = p->batch;
+    st.shape[1] = p->heads;
+    st.shape[2] = p->seq_len;
+  }
+  return rc;
+}
